@@ -1,0 +1,140 @@
+/*
+ * vkflame_rt.h — C ABI of libvkflame_rt.so, the B200 runtime under the shims.
+ *
+ * Replaces the reference's Vulkan runtime (runtime/device.h, runtime/buffer.h,
+ * runtime/dispatch.h) with a thin layer over the CUDA runtime.  Pointers are
+ * real CUDA device pointers; streams are cudaStream_t (hipStream_t values
+ * handed out by libamdhip64 are cudaStream_t); NULL means the legacy default
+ * stream.  Every entry point returns a vkflame status (0 = success) and also
+ * records it as the calling thread's last error.
+ *
+ * Entry points that exist in the reference keep its name and argument order
+ * (a caller that ignores the return value, as the reference's void functions
+ * imply, still links and runs).  Each is annotated with the reference
+ * declaration it replaces.
+ */
+#ifndef VKFLAME_RT_H
+#define VKFLAME_RT_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include "ggml_blocks.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define VKF_OK 0
+#define VKF_ERR_INVALID 1      /* bad shape / enum / NULL argument            */
+#define VKF_ERR_NOMEM 2        /* device allocation failed                      */
+#define VKF_ERR_BADPTR 3       /* pointer not device-accessible / out of range  */
+#define VKF_ERR_UNSUPPORTED 4  /* valid request this build does not implement   */
+#define VKF_ERR_CUDA 5         /* a CUDA call or kernel launch failed           */
+#define VKF_ERR_NO_DEVICE 6    /* no sm_100 device present                      */
+#define VKF_ERR_TIMEOUT 7      /* a kernel gave up a bounded wait (see below)   */
+
+/* Dtype codes of vkflame_dispatch_linear (runtime/dispatch.h:7-11). */
+#define VKF_DTYPE_FP32 0
+#define VKF_DTYPE_FP16 1
+#define VKF_DTYPE_INT8 2
+#define VKF_DTYPE_BF16 3
+#define VKF_DTYPE_FP16_FP32OUT 4
+
+/* Activation codes (kernels/linear_fp16.glsl:19, linear_int8.glsl:23). */
+#define VKF_ACT_NONE 0
+#define VKF_ACT_SILU 1
+#define VKF_ACT_RELU 2
+#define VKF_ACT_GELU_ERF 3
+
+/* Activation / output element types of vkflame_quant_linear. */
+#define VKF_X_F16 0
+#define VKF_X_Q8_1 1
+#define VKF_Y_F32 0
+#define VKF_Y_F16 1
+
+/* ---- device (runtime/device.h:39-42) ----------------------------------- */
+int vkflame_init(void);               /* idempotent; selects/validates the current device */
+void *vkflame_get_context(void);      /* opaque, non-NULL after init; never dereferenced by callers */
+void vkflame_shutdown(void);
+void vkflame_print_info(void);
+
+/* ---- memory (runtime/buffer.h:22-62; VKFBuffer* becomes a device pointer) */
+void *vkflame_alloc(size_t size);     /* cudaMalloc + allocation table; NULL on failure */
+int vkflame_free(void *ptr);
+int vkflame_memcpy_h2d(void *dst, const void *src, size_t size, size_t offset);
+int vkflame_memcpy_d2h(void *dst, const void *src, size_t size, size_t offset);
+int vkflame_memcpy_d2d(void *dst, const void *src, size_t size);
+int vkflame_memset(void *dst, int value, size_t size);
+/* Range lookup: any pointer inside a live vkflame_alloc block resolves to
+ * its base and size (the reference only matched block bases,
+ * shim/hip_runtime_shim.cpp:399-406). Returns VKF_ERR_BADPTR if unknown. */
+int vkflame_ptr_lookup(const void *ptr, void **base, size_t *size);
+/* Registers an allocation made elsewhere (e.g. by the hip shim) so range
+ * checks accept it. */
+int vkflame_register_alloc(void *base, size_t size);
+int vkflame_unregister_alloc(void *base);
+
+/* ---- dispatch (runtime/dispatch.h:51-92) -------------------------------- */
+
+/* runtime/dispatch.h:51-58.  Row-major D[MxN] = act(alpha * op(A) op(B) + beta * C).
+ * A is M x K (transA=1: stored K x M); B is K x N (transB=1: stored N x K).
+ * dtype selects element types as VKF_DTYPE_*; FP16_FP32OUT writes fp32 D.
+ * alpha/beta are host pointers to scalars of the compute type (fp32 for
+ * every dtype here; NULL means 1 and 0). */
+int vkflame_dispatch_linear(void *ctx, const void *A, const void *B, const void *C, void *D,
+                            int M, int N, int K, int dtype, int transA, int transB,
+                            int activation, const void *alpha, const void *beta, void *stream);
+
+/* runtime/dispatch.h:89-92.  Dequantise n_blocks blocks of quant_type to fp32
+ * (n_blocks counts blocks of the format: 32 values for Q4_0/Q4_1/Q5_0/Q8_0/Q8_1,
+ * 256 for Q4_K/Q5_K/Q6_K).  Bit-exact with kernels/dequant_*.glsl.
+ * The reference's src/dst were VKFBuffer*; here they are device pointers,
+ * and a sub-allocation offset inside them is honoured. */
+int vkflame_dispatch_dequant(void *ctx, const void *src, void *dst, uint32_t n_blocks, int quant_type);
+/* Same on an explicit stream. */
+int vkflame_dispatch_dequant_async(const void *src, void *dst, uint64_t n_blocks, int quant_type,
+                                   void *stream);
+
+/* Fused dequant + linear; replaces the reference's three-dispatch quantised
+ * mul_mat chain (shim/hip_runtime_shim.cpp:1102-1172).
+ *   W: N rows of K/QK blocks of wtype (Q4_0, Q8_0, Q4_K, Q5_K, Q6_K); ggml layout.
+ *   X: M x K activations, xtype VKF_X_F16 (row stride ldx elements) or
+ *      VKF_X_Q8_1 (row stride ldx blocks of 36 B; ldx = K/32 when packed).
+ *   Y: M x N, ytype VKF_Y_F32 or VKF_Y_F16, row stride ldy elements.
+ * Y[m,n] = sum_k X[m,k] * dequant(W)[n,k], fp32 accumulation.  M <= 8 runs
+ * the decode GEMV kernel; larger M the tensor-core GEMM. */
+int vkflame_quant_linear(const void *W, int wtype, const void *X, int xtype, void *Y, int ytype,
+                         int M, int N, int K, int64_t ldx, int64_t ldy, void *stream);
+
+/* On-device fp32 -> Q8_1 quantiser (no reference counterpart: the reference
+ * only decodes Q8_1, kernels/dequant_q8_1.glsl).  x is M x K fp32 (row stride
+ * ldx elements), y receives M rows of K/32 blocks (36 B each), packed.
+ * d = max|x|/127 over each 32-value block, q = clamp(round(x/d)) with
+ * round-half-away-from-zero, s = d*sum(q); d and s stored as fp16. */
+int vkflame_quantize_q8_1(const float *x, void *y, int M, int K, int64_t ldx, void *stream);
+
+/* linear_int8 with per-row and per-channel scales (kernels/linear_int8.glsl,
+ * with the defects of the reference's binding corrected):
+ *   acc[m,n] = sum_k X[m,k] * W[n,k]            (int32, bit-exact)
+ *   Y[m,n]   = fp16(act((acc * sx[m]) * sw[n] + bias[n]))
+ * X int8 M x K, W int8 N x K (both K contiguous), sx fp32[M] (NULL = 1),
+ * sw fp32[N] (NULL = 1), bias fp16[N] (NULL = none).  If acc_out is not NULL
+ * the raw int32 accumulators are also written (M x N). */
+int vkflame_linear_int8(const int8_t *X, const int8_t *W, const float *sx, const float *sw,
+                        const void *bias, void *Y, int32_t *acc_out, int M, int N, int K,
+                        int activation, void *stream);
+
+/* ---- diagnostics -------------------------------------------------------- */
+int vkflame_get_last_error(void);
+const char *vkflame_status_string(int status);
+/* Synchronises the current device and reports (and clears) the error bits
+ * kernels set when a bounded wait gave up: VKF_ERR_TIMEOUT if any was set. */
+int vkflame_check_kernel_errors(void);
+/* Number of kernels this library has launched since load (all devices). */
+uint64_t vkflame_kernel_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VKFLAME_RT_H */

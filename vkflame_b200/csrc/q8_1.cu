@@ -1,0 +1,85 @@
+// q8_1.cu — on-device Q8_1 activation quantiser and Q8_1 -> fp16 widening.
+//
+// The reference only decodes Q8_1 (kernels/dequant_q8_1.glsl); ggml produces
+// it on the device before its mul_mat_q kernels, so the B200 path provides
+// the producer.  One warp per 32-value block, one value per lane: the fp32
+// input is read fully coalesced and the 36-byte block written by 9 lanes.
+// The arithmetic is IEEE-rounded fp32 (no fast-math), so it matches the CPU
+// oracle (oracle_quantize_q8_1) bit for bit.
+
+#include "device_common.cuh"
+
+namespace vkf {
+namespace {
+
+__global__ void __launch_bounds__(256) quantize_q8_1_kernel(const float *__restrict__ x, uint8_t *__restrict__ y,
+                                                            int M, int K, int64_t ldx) {
+    const int lane = threadIdx.x & 31;
+    const int64_t blk = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int nbr = K / 32;
+    if (blk >= (int64_t)M * nbr) return;
+    const int64_t m = blk / nbr, b = blk % nbr;
+    const float v = x[m * ldx + b * 32 + lane];
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    int q = 0;
+    if (d != 0.0f) {
+        q = (int)roundf(__fdiv_rn(v, d));
+        q = max(-127, min(127, q));
+    }
+    int sum = q;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    uint8_t *out = y + blk * 36;
+    out[4 + lane] = (uint8_t)(int8_t)q;
+    if (lane == 0) {
+        __half hd = __float2half_rn(d), hs = __float2half_rn(__fmul_rn(d, (float)sum));
+        *reinterpret_cast<__half *>(out) = hd;
+        *reinterpret_cast<__half *>(out + 2) = hs;
+    }
+}
+
+// Q8_1 (M rows of K/32 blocks, row stride ldb blocks) -> fp16 M x K (row stride ldo).
+__global__ void __launch_bounds__(256) q8_1_to_f16_kernel(const uint8_t *__restrict__ src, __half *__restrict__ dst,
+                                                          int M, int K, int64_t ldb, int64_t ldo) {
+    const int lane = threadIdx.x & 31;
+    const int64_t blk = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int nbr = K / 32;
+    if (blk >= (int64_t)M * nbr) return;
+    const int64_t m = blk / nbr, b = blk % nbr;
+    const uint8_t *p = src + (m * ldb + b) * 36;
+    const float d = __half2float(*reinterpret_cast<const __half *>(p));
+    const int8_t q = reinterpret_cast<const int8_t *>(p + 4)[lane];
+    dst[m * ldo + b * 32 + lane] = __float2half_rn(__fmul_rn(d, (float)q));
+}
+
+}  // namespace
+
+int q8_1_to_f16(const void *src, void *dst, int M, int K, int64_t ldb, int64_t ldo, cudaStream_t stream) {
+    int64_t blocks = (int64_t)M * (K / 32);
+    if (blocks == 0) return VKF_OK;
+    q8_1_to_f16_kernel<<<(unsigned)((blocks + 7) / 8), 256, 0, stream>>>((const uint8_t *)src, (__half *)dst, M, K,
+                                                                            ldb, ldo);
+    return check_launch();
+}
+
+int quantize_q8_1_launch(const float *x, void *y, int M, int K, int64_t ldx, cudaStream_t stream) {
+    int64_t blocks = (int64_t)M * (K / 32);
+    if (blocks == 0) return VKF_OK;
+    quantize_q8_1_kernel<<<(unsigned)((blocks + 7) / 8), 256, 0, stream>>>(x, (uint8_t *)y, M, K, ldx);
+    return check_launch();
+}
+
+}  // namespace vkf
+
+extern "C" int vkflame_quantize_q8_1(const float *x, void *y, int M, int K, int64_t ldx, void *stream) {
+    if (M < 0 || K < 0 || K % 32 || ldx < K) return vkf::set_status(VKF_ERR_INVALID);
+    if (M == 0 || K == 0) return vkf::set_status(VKF_OK);
+    if (vkf::validate_device_range(x, ((size_t)(M - 1) * ldx + K) * 4) != VKF_OK ||
+        vkf::validate_device_range(y, (size_t)M * (K / 32) * 36) != VKF_OK || ((uintptr_t)x & 3) ||
+        ((uintptr_t)y & 1))
+        return vkf::set_status(VKF_ERR_BADPTR);
+    return vkf::set_status(vkf::quantize_q8_1_launch(x, y, M, K, ldx, (cudaStream_t)stream));
+}

@@ -1,0 +1,126 @@
+"""ctypes bindings of libvkflame_rt.so (include/vkflame_rt.h).
+
+Every wrapper takes raw device pointers (ints) and raises VkflameError on a
+non-zero status.  Streams are cudaStream_t values (0 = legacy default).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+from . import LIBS
+
+VKF_OK = 0
+STATUS = {0: "VKF_OK", 1: "VKF_ERR_INVALID", 2: "VKF_ERR_NOMEM", 3: "VKF_ERR_BADPTR",
+          4: "VKF_ERR_UNSUPPORTED", 5: "VKF_ERR_CUDA", 6: "VKF_ERR_NO_DEVICE", 7: "VKF_ERR_TIMEOUT"}
+
+Q4_0, Q4_1, Q8_0, Q5_0, Q4_K, Q5_K, Q6_K, Q8_1 = range(8)
+X_F16, X_Q8_1 = 0, 1
+Y_F32, Y_F16 = 0, 1
+DTYPE_FP32, DTYPE_FP16, DTYPE_INT8, DTYPE_BF16, DTYPE_FP16_FP32OUT = range(5)
+ACT_NONE, ACT_SILU, ACT_RELU, ACT_GELU_ERF = range(4)
+
+
+class VkflameError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        super().__init__(f"{what}: {STATUS.get(status, status)}")
+        self.status = status
+
+
+_SIGS = {
+    "vkflame_init": ([], C.c_int),
+    "vkflame_get_context": ([], C.c_void_p),
+    "vkflame_shutdown": ([], None),
+    "vkflame_print_info": ([], None),
+    "vkflame_alloc": ([C.c_size_t], C.c_void_p),
+    "vkflame_free": ([C.c_void_p], C.c_int),
+    "vkflame_memcpy_h2d": ([C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t], C.c_int),
+    "vkflame_memcpy_d2h": ([C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t], C.c_int),
+    "vkflame_memcpy_d2d": ([C.c_void_p, C.c_void_p, C.c_size_t], C.c_int),
+    "vkflame_memset": ([C.c_void_p, C.c_int, C.c_size_t], C.c_int),
+    "vkflame_ptr_lookup": ([C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_size_t)], C.c_int),
+    "vkflame_register_alloc": ([C.c_void_p, C.c_size_t], C.c_int),
+    "vkflame_unregister_alloc": ([C.c_void_p], C.c_int),
+    "vkflame_dispatch_linear": ([C.c_void_p] * 5 + [C.c_int] * 7 + [C.c_void_p] * 3, C.c_int),
+    "vkflame_dispatch_dequant": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_int], C.c_int),
+    "vkflame_dispatch_dequant_async": ([C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_void_p], C.c_int),
+    "vkflame_quant_linear": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                              C.c_int, C.c_int, C.c_int, C.c_int64, C.c_int64, C.c_void_p], C.c_int),
+    "vkflame_quantize_q8_1": ([C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int64, C.c_void_p], C.c_int),
+    "vkflame_linear_int8": ([C.c_void_p] * 7 + [C.c_int] * 4 + [C.c_void_p], C.c_int),
+    "vkflame_get_last_error": ([], C.c_int),
+    "vkflame_status_string": ([C.c_int], C.c_char_p),
+    "vkflame_check_kernel_errors": ([], C.c_int),
+    "vkflame_kernel_launch_count": ([], C.c_uint64),
+}
+
+
+def declared_symbols() -> list[str]:
+    return list(_SIGS)
+
+
+def load(path=None) -> C.CDLL:
+    p = path or LIBS["rt"]
+    if not p.exists():
+        raise ImportError(f"[vkflame_b200] {p} not built (run __graft_entry__.build())")
+    lib = C.CDLL(str(p), mode=C.RTLD_GLOBAL)
+    for name, (args, res) in _SIGS.items():
+        fn = getattr(lib, name, None)
+        if fn is None:
+            continue
+        fn.argtypes = args
+        fn.restype = res
+    return lib
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """The runtime library, initialised on a B200; raises otherwise."""
+    global _lib
+    if _lib is None:
+        l = load()
+        rc = l.vkflame_init()
+        if rc != VKF_OK:
+            raise VkflameError(rc, "vkflame_init (needs an sm_100 GPU)")
+        _lib = l
+    return _lib
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != VKF_OK:
+        raise VkflameError(rc, what)
+
+
+def dequant(src: int, dst: int, n_blocks: int, qtype: int, stream: int = 0) -> None:
+    _check(lib().vkflame_dispatch_dequant_async(src, dst, n_blocks, qtype, stream), "dequant")
+
+
+def quant_linear(W: int, wtype: int, X: int, xtype: int, Y: int, ytype: int, M: int, N: int, K: int,
+                 ldx: int, ldy: int, stream: int = 0) -> None:
+    _check(lib().vkflame_quant_linear(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, stream), "quant_linear")
+
+
+def quantize_q8_1(x: int, y: int, M: int, K: int, ldx: int, stream: int = 0) -> None:
+    _check(lib().vkflame_quantize_q8_1(x, y, M, K, ldx, stream), "quantize_q8_1")
+
+
+def linear_int8(X: int, W: int, sx: int, sw: int, bias: int, Y: int, acc: int, M: int, N: int, K: int,
+                act: int = 0, stream: int = 0) -> None:
+    _check(lib().vkflame_linear_int8(X, W, sx, sw, bias, Y, acc, M, N, K, act, stream), "linear_int8")
+
+
+def dispatch_linear(A: int, B: int, C_: int, D: int, M: int, N: int, K: int, dtype: int, transA: int = 0,
+                    transB: int = 0, act: int = 0, alpha=None, beta=None, stream: int = 0) -> None:
+    a = C.byref(C.c_float(alpha)) if alpha is not None else None
+    b = C.byref(C.c_float(beta)) if beta is not None else None
+    _check(lib().vkflame_dispatch_linear(None, A, B, C_, D, M, N, K, dtype, transA, transB, act, a, b, stream),
+           "dispatch_linear")
+
+
+def check_kernel_errors() -> None:
+    _check(lib().vkflame_check_kernel_errors(), "kernel error bits")
+
+
+def launch_count() -> int:
+    return lib().vkflame_kernel_launch_count()
