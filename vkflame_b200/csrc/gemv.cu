@@ -7,51 +7,71 @@
 // GEMM (shim/hip_runtime_shim.cpp:1102-1172, kernels/linear_fp16_fp32out.glsl).
 // Here the packed blocks are read once from HBM and decoded in registers.
 //
-// Structure (per CTA, 160 threads):
-//   warp 4      producer: one TMA bulk copy (cp.async.bulk) per weight row per
-//               K-step into an NST-deep shared-memory ring, plus the K-step's
-//               activations, completion tracked by mbarrier transaction bytes;
-//               weights are marked L2 evict-first (streamed once).
-//   warps 0..3  consumers: each owns 32 rows (two 16-row MMA groups) of the
-//               128-row tile, decodes blocks into m16n8k16 fragments
-//               (gemv_q.cuh) and accumulates in fp32 registers.  The MMA's
-//               8-wide N dimension carries the M <= 8 batch columns.
-// Scheduling is stream-K: the (tile, K-step) iteration space is split
-// evenly over a grid sized to fill the GPU, so any N balances across all
-// SMs.  A tile split between CTAs is finished by the last contributor,
-// which sums the partials in CTA order (deterministic) from scratch memory.
+// Measured on B200 (copy microbenchmarks): streaming reads reach ~7.1 TB/s
+// when each request run is kilobytes long, but a 128-row x 144..272-byte
+// K-step (the natural MMA tile of a ggml row-major matrix) held DRAM to
+// 2.6-4.4 TB/s.  The kernel therefore works on items of 16 rows x a K-range
+// of up to ~3 KB of each row (the whole row for K = 5120 Q4_K):
+//
+//   warp CW       producer: one TMA bulk copy per row per item into an
+//                 NST-deep ring, completion by mbarrier transaction bytes.
+//   warps 0..CW-1 consumers: split the item's work units (256 values, or a
+//                 128-value half super-block for K-quants) between them,
+//                 decode into m16n8k16 fragments (gemv_q.cuh: A = the 16
+//                 weight rows, N = the M <= 8 activation columns) and keep a
+//                 per-warp fp32 accumulator; at the end of a row block the CW
+//                 partials are reduced through shared memory.
+//
+// The activations X (M x K fp16) stay resident in shared memory for the whole
+// CTA, stored permuted in fragment order; the fp32 sums of every 32-value
+// sub-block (hi + lo fp16) are precomputed next to them for the K-quant
+// min-term MMA.  Scheduling is stream-K over the (row block, K-range) items:
+// the iteration space is split evenly over one CTA per SM, and a row block
+// split between CTAs is finished by its last contributor, which sums the
+// partials in CTA order (deterministic) from scratch memory.  Batch columns
+// that do not fit the resident budget are processed in groups by the caller.
 
 #include "gemv_q.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace vkf {
 namespace gemv {
 
+constexpr int CW = 16;                // consumer warps
+constexpr int NT = 32 * (CW + 1);
+constexpr int NST = 3;                // ring depth
+constexpr int ROW_BUDGET = 3040;      // max bytes of one row per item
+constexpr int X_BUDGET = 80 * 1024;   // resident activations + sums
+constexpr int SMEM_MAX = 227 * 1024;
+constexpr int ZERO_BYTES = 1024;      // zero activations / sums for columns >= M
+
 struct Args {
     const uint8_t *W;
-    const uint8_t *X;  // fp16 activations, rows 16-byte aligned
+    const uint8_t *X;  // fp16, rows 16-byte aligned
     void *Y;
     int M, N, K;
-    int64_t ldx_bytes;  // X row stride in bytes (multiple of 16)
-    int64_t ldy;        // Y row stride in elements
-    int64_t row_bytes;  // W row stride in bytes
-    int T, S;           // tiles, K-steps per tile
-    int64_t I;          // T * S
-    int G;              // grid size
-    float *ws;          // partial tiles: [G][2][1024] floats
-    int *cnt;           // per-tile arrival counters (zero between launches)
+    int64_t ldx_bytes, ldy, row_bytes;
+    int units;         // 256-value units per row (the last may be partial for 32-value blocks)
+    int upi;           // units per item (the last item of a row block may have fewer)
+    int S;             // items per row block
+    int T;             // row blocks of 16 rows
+    int64_t I;         // T * S
+    int G;             // grid
+    int rpb;           // smem pitch of one row's bytes in a stage
+    int xpr;           // smem pitch of one resident activation row
+    int xsp;           // smem pitch of one column's sub-block sums
+    int stage_bytes;
+    float *ws;         // partials: [G][2][128] floats
+    int *cnt;          // per-row-block arrival counters (zero between launches)
     unsigned *err;
     int y_f16;
 };
 
-constexpr int NT = 160;
-constexpr int PARTIAL_FLOATS = 4 * 2 * 32 * 4;  // warps x groups x lanes x 4
-
 __device__ __forceinline__ int cta_of(int64_t i, const Args &a) { return (int)(((i + 1) * a.G - 1) / a.I); }
 __device__ __forceinline__ int64_t first_iter(int c, const Args &a) { return (int64_t)c * a.I / a.G; }
-
-__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory"); }
 
 __device__ __forceinline__ void store_y(const Args &a, int m, int n, float v) {
     if (m < a.M && n < a.N) {
@@ -60,229 +80,245 @@ __device__ __forceinline__ void store_y(const Args &a, int m, int n, float v) {
     }
 }
 
-template <int QT, int NST>
-__global__ void __launch_bounds__(NT, 2) gemv_kernel(const __grid_constant__ Args a) {
-    using Gm = Geo<QT>;
-    constexpr int QK = Fmt<QT>::QK, BB = Fmt<QT>::BB;
+template <int QT>
+__global__ void __launch_bounds__(NT, 1) gemv_kernel(const __grid_constant__ Args a) {
+    constexpr int QK = Fmt<QT>::QK, BB = Fmt<QT>::BB, PARTS = Fmt<QT>::PARTS;
+    constexpr int UB = (256 / QK) * BB;  // bytes of one 256-value unit of a row
+    constexpr bool KQ = QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K;  // has a min term
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + NST * Gm::STAGE);
+    uint8_t *xs = smem;                                       // M x xpr, permuted fp16
+    uint8_t *sums = xs + a.M * a.xpr;                         // M x xsp (K-quants)
+    uint8_t *zero = sums + a.M * a.xsp;                       // ZERO_BYTES of zeros
+    uint8_t *ring = zero + ZERO_BYTES;                        // NST x stage_bytes
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + NST * a.stage_bytes);
     uint64_t *empty = full + NST;
-    int *flag = reinterpret_cast<int *>(empty + NST);
+    float *red = reinterpret_cast<float *>(empty + NST + 2);  // CW x 32 x 4
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cta = blockIdx.x;
     const int64_t it0 = first_iter(cta, a), it1 = first_iter(cta + 1, a);
 
+    for (int i = threadIdx.x; i < ZERO_BYTES / 16; i += NT) reinterpret_cast<uint4 *>(zero)[i] = make_uint4(0, 0, 0, 0);
     if (threadIdx.x == 0) {
         for (int s = 0; s < NST; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 4);
+            mbar_init(&empty[s], CW);
         }
         fence_mbar_init();
     }
-    // Activation columns >= M are never copied: make them zero once.
-    for (int s = 0; s < NST; ++s)
-        for (int i = threadIdx.x; i < (8 - a.M) * (XP / 16); i += NT) {
-            int col = a.M + i / (XP / 16);
-            reinterpret_cast<uint4 *>(smem + s * Gm::STAGE + TILE_ROWS * Gm::RP + col * XP)[i % (XP / 16)] =
-                make_uint4(0, 0, 0, 0);
-        }
     __syncthreads();
 
-    if (warp == 4) {
+    if (warp == CW) {
         // ---------------- producer ----------------
-        const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
         int n = 0;
         for (int64_t it = it0; it < it1; ++it, ++n) {
             const int s = n % NST;
             const uint32_t ph = (uint32_t)(n / NST) & 1u;
             if (n >= NST && !mbar_wait(&empty[s], ph ^ 1u, a.err)) break;
-            const int tile = (int)(it / a.S), step = (int)(it % a.S);
-            const int nval = min(KS, a.K - step * KS);
-            const int wbytes = nval / QK * BB;
-            uint8_t *st = smem + s * Gm::STAGE;
-            uint32_t srow[4], ssz[4];
-            const uint8_t *sbase[4];
-            uint32_t mine = 0;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int r = lane + 32 * i;
-                const int row = tile * TILE_ROWS + r;
-                ssz[i] = 0;
-                srow[i] = r;
-                if (row < a.N) {
-                    const uint8_t *src = a.W + (int64_t)row * a.row_bytes + (int64_t)step * Gm::STEP_BYTES;
-                    const uint32_t off = (uint32_t)((uintptr_t)src & 15);
-                    sbase[i] = src - off;
-                    ssz[i] = (off + wbytes + 15) & ~15u;
-                    mine += ssz[i];
-                }
+            const int tile = (int)(it / a.S), step = (int)(it - (int64_t)tile * a.S);
+            const int u0 = step * a.upi, nu = min(a.upi, a.units - u0);
+            // Bytes of this item's units in one row (a partial last unit of a
+            // 32-value-block format holds only the blocks that exist), widened
+            // to whole 16-byte granules: a 16-byte aligned granule never
+            // crosses a page, so the few bytes read either side are mapped.
+            const int64_t b0 = (int64_t)u0 * UB;
+            const int64_t b1 = (int64_t)(u0 + nu) * UB < a.row_bytes ? (int64_t)(u0 + nu) * UB : a.row_bytes;
+            const int row = tile * 16 + lane;
+            uint32_t sz = 0;
+            const uint8_t *src = nullptr;
+            if (lane < 16 && row < a.N) {
+                const uint8_t *p = a.W + (int64_t)row * a.row_bytes + b0;
+                const uint32_t off = (uint32_t)((uintptr_t)p & 15);
+                src = p - off;
+                sz = (uint32_t)((off + (b1 - b0) + 15) & ~15);
             }
-            uint32_t xsz = 0;
-            const uint8_t *xsrc = nullptr;
-            if (lane < a.M) {
-                xsrc = a.X + (int64_t)lane * a.ldx_bytes + (int64_t)step * KS * 2;
-                xsz = (nval * 2 + 15) & ~15u;
-                mine += xsz;
-            }
-            uint32_t total = mine;
+            uint32_t total = sz;
 #pragma unroll
             for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
             if (lane == 0) mbar_arrive_expect_tx(&full[s], total);
             __syncwarp();
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-                if (ssz[i]) bulk_g2s(st + srow[i] * Gm::RP, sbase[i], ssz[i], &full[s], pol_w);
-            if (xsz) bulk_g2s(st + TILE_ROWS * Gm::RP + lane * XP, xsrc, xsz, &full[s], pol_x);
+            if (sz) bulk_g2s(ring + s * a.stage_bytes + lane * a.rpb, src, sz, &full[s]);
         }
         return;
     }
 
     // ---------------- consumers ----------------
+    // Resident activations, permuted (x0, x2, x1, x3) per group of four.
+    {
+        const int groups = a.K / 4;
+        for (int i = threadIdx.x; i < a.M * groups; i += CW * 32) {
+            const int m = i / groups, q = i - m * groups;
+            const uint2 v = *reinterpret_cast<const uint2 *>(a.X + (int64_t)m * a.ldx_bytes + q * 8);
+            *reinterpret_cast<uint2 *>(xs + m * a.xpr + q * 8) =
+                make_uint2(prmt(v.x, v.y, 0x5410), prmt(v.x, v.y, 0x7632));
+        }
+    }
+    consumer_bar();
+    if constexpr (KQ) {
+        // fp32 sum of each 32-value sub-block, split hi + lo fp16, laid out as
+        // the min MMA's B fragment: [super-block][t] = (hi 2t, 2t+1 | lo 2t, 2t+1)
+        const int nsub = a.K / 32;
+        for (int i = threadIdx.x; i < a.M * nsub; i += CW * 32) {
+            const int m = i / nsub, j = i - m * nsub;
+            const __half *xr = reinterpret_cast<const __half *>(xs + m * a.xpr) + j * 32;
+            float sum = 0.f;
+#pragma unroll 8
+            for (int k = 0; k < 32; ++k) sum += __half2float(xr[k]);
+            const __half hi = __float2half_rn(sum);
+            const __half lo = __float2half_rn(sum - __half2float(hi));
+            __half *o = reinterpret_cast<__half *>(sums + m * a.xsp + (j / 8) * 32 + ((j % 8) / 2) * 8) + (j & 1);
+            o[0] = hi;
+            o[2] = lo;
+        }
+        consumer_bar();
+    }
+
     const int g = lane >> 2, t = lane & 3;
-    float acc[2][4];
-#pragma unroll
-    for (int r = 0; r < 2; ++r) zero4(acc[r]);
-    const int first_tile = (int)(it0 / a.S);
+    const uint8_t *xg = g < a.M ? xs + g * a.xpr : nullptr;
+    const uint8_t *sg = g < a.M ? sums + g * a.xsp : nullptr;
     // After a bounded wait gives up (error bit already set) the warp keeps
     // walking the same iterations without waiting or computing, so every
     // consumer warp still reaches the same named barriers.
     bool ok = true;
+    float acc[4];
+    zero4(acc);
+    const int first_tile = (int)(it0 / a.S);
     int n = 0;
     for (int64_t it = it0; it < it1; ++it, ++n) {
         const int s = n % NST;
         const uint32_t ph = (uint32_t)(n / NST) & 1u;
         if (ok) ok = mbar_wait(&full[s], ph, a.err);
-        const int tile = (int)(it / a.S), step = (int)(it % a.S);
-        const int nval = min(KS, a.K - step * KS);
-        const uint8_t *st = smem + s * Gm::STAGE;
-        const uint8_t *xc = st + TILE_ROWS * Gm::RP + g * XP;
-#pragma unroll
-        for (int rg = 0; rg < 2; ++rg) {
-            if (!ok) break;
-            const int r_a = warp * 32 + rg * 16 + g, r_b = r_a + 8;
-            const int64_t row_a = (int64_t)tile * TILE_ROWS + r_a, row_b = row_a + 8;
-            const uintptr_t ga = (uintptr_t)a.W + row_a * a.row_bytes + (int64_t)step * Gm::STEP_BYTES;
-            const uintptr_t gb = (uintptr_t)a.W + row_b * a.row_bytes + (int64_t)step * Gm::STEP_BYTES;
-            Step<QT>::run(st + r_a * Gm::RP + (ga & 15), st + r_b * Gm::RP + (gb & 15), xc, t, nval / 32, acc[rg]);
+        const int tile = (int)(it / a.S), step = (int)(it - (int64_t)tile * a.S);
+        const int u0 = step * a.upi, nu = min(a.upi, a.units - u0);
+        if (ok) {
+            const uint8_t *st = ring + s * a.stage_bytes;
+            const int64_t row_a = (int64_t)tile * 16 + g, row_b = row_a + 8;
+            const uintptr_t ga = (uintptr_t)a.W + row_a * a.row_bytes + (int64_t)u0 * UB;
+            const uintptr_t gb = (uintptr_t)a.W + row_b * a.row_bytes + (int64_t)u0 * UB;
+            const uint8_t *ra = st + g * a.rpb + (ga & 15), *rb = st + (g + 8) * a.rpb + (gb & 15);
+            for (int wi = warp; wi < nu * PARTS; wi += CW) {
+                const int u = wi / PARTS, part = wi - u * PARTS;
+                const int kv = (u0 + u) * 256;
+                const int nblk = min(8, (a.K - kv) / 32);
+                const uint8_t *xc = xg ? xg + kv * 2 : zero;
+                const uint8_t *xsum = sg ? sg + (u0 + u) * 32 : zero;
+                Step<QT>::run(ra + u * UB, rb + u * UB, xc, xsum, t, part, nblk, acc);
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
 
         if (step != a.S - 1 && it + 1 != it1) continue;
 
-        // ---- tile epilogue ----
+        // ---- row-block epilogue: reduce the CW warp partials ----
+        reinterpret_cast<float4 *>(red)[warp * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        consumer_bar();
+        if (warp == 0) {
+            float o[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int w = 0; w < CW; ++w) {
+                const float4 v = reinterpret_cast<const float4 *>(red)[w * 32 + lane];
+                o[0] += v.x;
+                o[1] += v.y;
+                o[2] += v.z;
+                o[3] += v.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[i] = o[i];
+        }
         const int64_t tb = (int64_t)tile * a.S;
         const bool whole = tb >= it0 && tb + a.S <= it1;
-        float out[2][4];
-        bool write = true;
-        if (whole) {
-#pragma unroll
-            for (int r = 0; r < 2; ++r)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) out[r][i] = acc[r][i];
-        } else {
+        bool write = warp == 0;
+        if (!whole && warp == 0) {
             const int slot = tile == first_tile ? 0 : 1;
-            float *mine = a.ws + ((int64_t)cta * 2 + slot) * PARTIAL_FLOATS;
-#pragma unroll
-            for (int r = 0; r < 2; ++r)
-                reinterpret_cast<float4 *>(mine)[(warp * 2 + r) * 32 + lane] =
-                    make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+            reinterpret_cast<float4 *>(a.ws + ((int64_t)cta * 2 + slot) * 128)[lane] =
+                make_float4(acc[0], acc[1], acc[2], acc[3]);
             __threadfence();
-            consumer_bar();
+            __syncwarp();
             const int c_first = cta_of(tb, a), c_last = cta_of(tb + a.S - 1, a);
-            if (threadIdx.x == 0) {
-                int old = atomicAdd(&a.cnt[tile], 1);
-                *flag = (old == c_last - c_first);
-            }
-            consumer_bar();
-            write = *flag != 0;
+            int last = 0;
+            if (lane == 0) last = atomicAdd(&a.cnt[tile], 1) == c_last - c_first;
+            last = __shfl_sync(0xffffffffu, last, 0);
+            write = last != 0;
             if (write) {
                 __threadfence();
-#pragma unroll
-                for (int r = 0; r < 2; ++r) zero4(out[r]);
+                zero4(acc);
+#pragma unroll 4
                 for (int c = c_first; c <= c_last; ++c) {
                     const int cslot = (tile == (int)(first_iter(c, a) / a.S)) ? 0 : 1;
-                    const float *p = a.ws + ((int64_t)c * 2 + cslot) * PARTIAL_FLOATS;
-#pragma unroll
-                    for (int r = 0; r < 2; ++r) {
-                        float4 v = __ldcg(reinterpret_cast<const float4 *>(p) + (warp * 2 + r) * 32 + lane);
-                        out[r][0] += v.x;
-                        out[r][1] += v.y;
-                        out[r][2] += v.z;
-                        out[r][3] += v.w;
-                    }
+                    const float4 v =
+                        __ldcg(reinterpret_cast<const float4 *>(a.ws + ((int64_t)c * 2 + cslot) * 128) + lane);
+                    acc[0] += v.x;
+                    acc[1] += v.y;
+                    acc[2] += v.z;
+                    acc[3] += v.w;
                 }
-                if (threadIdx.x == 0) atomicExch(&a.cnt[tile], 0);
+                if (lane == 0) atomicExch(&a.cnt[tile], 0);
             }
-            consumer_bar();  // `flag` is reused by the next tile
         }
         if (write) {
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const int row = tile * TILE_ROWS + warp * 32 + r * 16 + g;
-                store_y(a, 2 * t, row, out[r][0]);
-                store_y(a, 2 * t + 1, row, out[r][1]);
-                store_y(a, 2 * t, row + 8, out[r][2]);
-                store_y(a, 2 * t + 1, row + 8, out[r][3]);
-            }
+            const int row = tile * 16 + g;
+            store_y(a, 2 * t, row, acc[0]);
+            store_y(a, 2 * t + 1, row, acc[1]);
+            store_y(a, 2 * t, row + 8, acc[2]);
+            store_y(a, 2 * t + 1, row + 8, acc[3]);
         }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) zero4(acc[r]);
+        zero4(acc);
+        consumer_bar();  // `red` is reused by the next row block
     }
 }
 
 template <int QT>
 struct Launcher {
-    static constexpr int NST = 4;
-    static size_t smem_bytes() { return (size_t)NST * Geo<QT>::STAGE + 2 * NST * sizeof(uint64_t) + 16; }
-    static int occupancy() {
-        static int occ[64] = {0};
+    static constexpr int QK = Fmt<QT>::QK, BB = Fmt<QT>::BB;
+    static constexpr int UB = (256 / QK) * BB;
+    static constexpr bool KQ = QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K;
+    static int launch(Args &a, int sms, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap) {
+        a.units = (a.K + 255) / 256;
+        a.xpr = ((a.K * 2 + 95) / 128) * 128 + 32;  // pitch = 8 banks mod 32: conflict-free fragment loads
+        a.xsp = KQ ? ((a.K / 256) * 32 + 15) / 16 * 16 : 0;
+        const int fixed = a.M * (a.xpr + a.xsp) + ZERO_BYTES + 2 * NST * 8 + 16 + CW * 32 * 16;
+        const int row_avail = (SMEM_MAX - fixed) / (NST * 16) - 32;  // room for padding and misalignment
+        const int umax = std::min(ROW_BUDGET, row_avail) / UB;
+        if (umax < 1) return VKF_ERR_UNSUPPORTED;
+        a.S = (a.units + umax - 1) / umax;
+        a.upi = (a.units + a.S - 1) / a.S;
+        a.S = (a.units + a.upi - 1) / a.upi;
+        a.T = (a.N + 15) / 16;
+        a.I = (int64_t)a.T * a.S;
+        const int ng = ((a.upi * UB + 15) / 16 + 1) | 1;  // odd granule count: rows 4 banks apart
+        a.rpb = ng * 16;
+        a.stage_bytes = 16 * a.rpb;
+        const size_t smem = (size_t)fixed + NST * (size_t)a.stage_bytes;
+        if (smem > SMEM_MAX) return VKF_ERR_UNSUPPORTED;
+        static bool attr_set[64] = {false};
         int dev = 0;
         cudaGetDevice(&dev);
-        if (dev < 64 && occ[dev]) return occ[dev];
-        cudaFuncSetAttribute(gemv_kernel<QT, NST>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes());
-        int o = 0;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_kernel<QT, NST>, NT, smem_bytes());
-        if (o < 1) o = 1;
-        if (dev < 64) occ[dev] = o;
-        return o;
-    }
-    static int launch(Args &a, int sms, cudaStream_t stream, void *scratch_override, size_t scratch_cap) {
-        a.T = (a.N + TILE_ROWS - 1) / TILE_ROWS;
-        a.S = (a.K + KS - 1) / KS;
-        a.I = (int64_t)a.T * a.S;
-        int64_t g = (int64_t)sms * occupancy();
-        a.G = (int)std::min<int64_t>(g, a.I);
-        size_t cnt_bytes = ((size_t)a.T * sizeof(int) + 255) & ~size_t(255);
-        size_t need = cnt_bytes + (size_t)a.G * 2 * PARTIAL_FLOATS * sizeof(float);
-        uint8_t *scr;
-        if (scratch_override) {
-            if (need > scratch_cap) return VKF_ERR_INVALID;
-            scr = (uint8_t *)scratch_override;
-        } else {
-            scr = (uint8_t *)stream_scratch(stream, need);
-            if (!scr) return VKF_ERR_NOMEM;
+        if (dev < 64 && !attr_set[dev]) {
+            cudaFuncSetAttribute(gemv_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX);
+            attr_set[dev] = true;
         }
-        a.cnt = reinterpret_cast<int *>(scr);
-        a.ws = reinterpret_cast<float *>(scr + cnt_bytes);
-        gemv_kernel<QT, NST><<<a.G, NT, smem_bytes(), stream>>>(a);
+        a.G = (int)std::max<int64_t>(1, std::min<int64_t>(sms, a.I));
+        if ((size_t)a.G * 2 * 128 > ws_cap || (size_t)a.T > cnt_cap) return VKF_ERR_INVALID;
+        a.ws = ws;
+        a.cnt = cnt;
+        gemv_kernel<QT><<<a.G, NT, smem, stream>>>(a);
         return check_launch();
     }
 };
 
 }  // namespace gemv
 
-// Size of the scratch a GEMV call needs (counters + partial tiles).
-size_t gemv_scratch_bytes(int N, int sms, int occ) {
-    int T = (N + gemv::TILE_ROWS - 1) / gemv::TILE_ROWS;
-    size_t cnt_bytes = ((size_t)T * sizeof(int) + 255) & ~size_t(255);
-    return cnt_bytes + (size_t)sms * occ * 2 * gemv::PARTIAL_FLOATS * sizeof(float);
+// Batch columns per launch so the resident activations fit the budget.
+int gemv_cols_per_launch(int K) {
+    const size_t per = (size_t)K * 2 + 160 + (size_t)K / 8;
+    return (int)std::max<size_t>(1, std::min<size_t>(8, gemv::X_BUDGET / per));
 }
+size_t gemv_counters(int N) { return (size_t)(N + 15) / 16; }
+size_t gemv_ws_floats(int sms) { return (size_t)sms * 2 * 128; }
 
 // X: fp16, rows 16-byte aligned (ldx_bytes multiple of 16).  Checked by caller.
-int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void *Y, int y_f16, int64_t ldy,
-                int M, int N, int K, cudaStream_t stream, void *scratch, size_t scratch_cap) {
+int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void *Y, int y_f16, int64_t ldy, int M,
+                int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap) {
     DeviceState *ds = device_state();
     if (!ds) return VKF_ERR_NO_DEVICE;
     gemv::Args a{};
@@ -299,11 +335,11 @@ int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void
     a.y_f16 = y_f16;
     const int sms = ds->sm_count;
     switch (wtype) {
-    case VKF_DEQUANT_Q4_0: return gemv::Launcher<VKF_DEQUANT_Q4_0>::launch(a, sms, stream, scratch, scratch_cap);
-    case VKF_DEQUANT_Q8_0: return gemv::Launcher<VKF_DEQUANT_Q8_0>::launch(a, sms, stream, scratch, scratch_cap);
-    case VKF_DEQUANT_Q4_K: return gemv::Launcher<VKF_DEQUANT_Q4_K>::launch(a, sms, stream, scratch, scratch_cap);
-    case VKF_DEQUANT_Q5_K: return gemv::Launcher<VKF_DEQUANT_Q5_K>::launch(a, sms, stream, scratch, scratch_cap);
-    case VKF_DEQUANT_Q6_K: return gemv::Launcher<VKF_DEQUANT_Q6_K>::launch(a, sms, stream, scratch, scratch_cap);
+    case VKF_DEQUANT_Q4_0: return gemv::Launcher<VKF_DEQUANT_Q4_0>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    case VKF_DEQUANT_Q8_0: return gemv::Launcher<VKF_DEQUANT_Q8_0>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    case VKF_DEQUANT_Q4_K: return gemv::Launcher<VKF_DEQUANT_Q4_K>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    case VKF_DEQUANT_Q5_K: return gemv::Launcher<VKF_DEQUANT_Q5_K>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    case VKF_DEQUANT_Q6_K: return gemv::Launcher<VKF_DEQUANT_Q6_K>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
     default: return VKF_ERR_UNSUPPORTED;
     }
 }

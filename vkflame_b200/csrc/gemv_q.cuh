@@ -1,26 +1,22 @@
-// gemv_q.cuh — per-format decode of one K-step of a 16-row group into
+// gemv_q.cuh — per-format decode of one work unit of a 16-row group into
 // m16n8k16 tensor-core fragments, for the decode GEMV (M <= 8).
-//
-// Layout of one K-step (256 values of K) in shared memory: each weight row's
-// ggml blocks for that step, copied verbatim by TMA (row slot pitch RP,
-// starting `off` bytes in, where off = global address & 15); and the 256
-// activations of each of the 8 batch columns (fp16, 16-byte aligned).
 //
 // Fragment mapping.  The 16 k-slots of each MMA cover 16 consecutive values
 // of one 32-value (sub-)block; thread t (= lane & 3) owns the 4 values
 // 4t..4t+3, so its weight bytes are one 32-bit word.  Within the MMA, slot
 // (2t, 2t+1) holds values (4t, 4t+2) and slot (2t+8, 2t+9) holds (4t+1, 4t+3):
 // exactly the half2 pairs a single LOP3 extracts from bytes (0,2) and (1,3)
-// of the word.  The B fragment (activations) uses the same permutation, so
-// the dot product is unchanged.
+// of the word.  The activations (B fragment) are stored with the same
+// permutation, so the dot product is unchanged.
 //
 // Exactness.  The A operand is always an integer that fp16 represents
 // exactly: q-8 (Q4_0), q (Q8_0), sc*q (Q4_K, <= 945; Q5_K, <= 1953), q-32
-// (Q6_K).  They are produced from "1024 + code" fp16 bit patterns with one
-// fp16 FMA whose exact result is that integer, so the single rounding is
-// exact.  Products with fp16 activations are exact in the fp32 accumulator;
-// the per-block fp32 scales (d, d*sc, dmin) are applied to the fp32 partial
-// sums.  The only roundings are fp32 accumulation.
+// (Q6_K), m (K-quant mins).  They are produced from "1024 + code" fp16 bit
+// patterns with one fp16 operation whose exact result is that integer, so the
+// single rounding is exact.  Products with fp16 activations are exact in the
+// fp32 accumulator; the per-block fp32 scales (d, d*sc, dmin) are applied to
+// the fp32 partial sums.  The only roundings are fp32 accumulation (and the
+// hi + lo fp16 split of the K-quant sub-block sums, exact to ~2^-22).
 #pragma once
 
 #include "device_common.cuh"
@@ -28,22 +24,13 @@
 namespace vkf {
 namespace gemv {
 
-constexpr int KS = 256;          // values of K per step
-constexpr int TILE_ROWS = 128;   // rows per tile: 4 consumer warps x 2 groups x 16
-constexpr int XP = KS * 2 + 16;  // smem bytes per activation column slot
-
+// QK values per block, BB bytes per block, PARTS work units per 256 values.
 template <int QT> struct Fmt;
-template <> struct Fmt<VKF_DEQUANT_Q4_0> { static constexpr int QK = 32, BB = 18; };
-template <> struct Fmt<VKF_DEQUANT_Q8_0> { static constexpr int QK = 32, BB = 34; };
-template <> struct Fmt<VKF_DEQUANT_Q4_K> { static constexpr int QK = 256, BB = 144; };
-template <> struct Fmt<VKF_DEQUANT_Q5_K> { static constexpr int QK = 256, BB = 176; };
-template <> struct Fmt<VKF_DEQUANT_Q6_K> { static constexpr int QK = 256, BB = 210; };
-
-template <int QT> struct Geo {
-    static constexpr int STEP_BYTES = (KS / Fmt<QT>::QK) * Fmt<QT>::BB;  // bytes of one row per step
-    static constexpr int RP = ((STEP_BYTES + 15) / 16) * 16 + 16;       // row slot pitch (room for off)
-    static constexpr int STAGE = TILE_ROWS * RP + 8 * XP;
-};
+template <> struct Fmt<VKF_DEQUANT_Q4_0> { static constexpr int QK = 32, BB = 18, PARTS = 1; };
+template <> struct Fmt<VKF_DEQUANT_Q8_0> { static constexpr int QK = 32, BB = 34, PARTS = 1; };
+template <> struct Fmt<VKF_DEQUANT_Q4_K> { static constexpr int QK = 256, BB = 144, PARTS = 2; };
+template <> struct Fmt<VKF_DEQUANT_Q5_K> { static constexpr int QK = 256, BB = 176, PARTS = 2; };
+template <> struct Fmt<VKF_DEQUANT_Q6_K> { static constexpr int QK = 256, BB = 210, PARTS = 2; };
 
 // fp16 constants (bit patterns)
 constexpr uint32_t H2_MAGIC = 0x64006400u;  // (1024, 1024)
@@ -63,11 +50,14 @@ __device__ __forceinline__ uint32_t lop3_and_xor(uint32_t a, uint32_t b, uint32_
     return r;
 }
 
-// B fragment of 16 k-values starting at activation column base `xcol` + k0.
+// B fragment of the 16 k-values starting at k0 of one activation column.
+// The column is stored permuted within each group of four values as
+// (x0, x2, x1, x3), so thread t's fragment (b0 = (x[4t], x[4t+2]),
+// b1 = (x[4t+1], x[4t+3])) is one 64-bit load.
 __device__ __forceinline__ void xfrag(const uint8_t *xcol, int k0, int t, uint32_t &b0, uint32_t &b1) {
     uint2 v = *reinterpret_cast<const uint2 *>(xcol + (k0 + 4 * t) * 2);
-    b0 = prmt(v.x, v.y, 0x5410);  // (x0, x2)
-    b1 = prmt(v.x, v.y, 0x7632);  // (x1, x3)
+    b0 = v.x;
+    b1 = v.y;
 }
 
 __device__ __forceinline__ uint32_t ld32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
@@ -76,15 +66,18 @@ __device__ __forceinline__ float hbits(const uint8_t *p) { return half_bits_to_f
 
 __device__ __forceinline__ void zero4(float (&p)[4]) { p[0] = p[1] = p[2] = p[3] = 0.f; }
 
-// Accumulates one K-step for rows (g, g+8) of a 16-row group.
-//   ra, rb: smem start of the step's blocks for rows g and g+8
-//   xc:     smem activation slot of column g (16-byte aligned, step-local k)
-//   nblk:   32-value blocks present in this step (tail steps of Q4_0/Q8_0)
+// Accumulates one work unit for rows (g, g+8) of a 16-row group.
+//   ra, rb: smem start of the unit's blocks for rows g and g+8 (a 256-value
+//           unit: one super-block, or eight 32-value blocks)
+//   xc:     permuted activations of column g at the unit's first value
+//   xs:     (Q4_K, Q5_K) sub-block sums of column g for this super-block
+//   part:   (K-quants) which 128-value half of the super-block
+//   nblk:   32-value blocks present (tail unit of Q4_0 / Q8_0)
 template <int QT> struct Step;
 
 template <> struct Step<VKF_DEQUANT_Q4_0> {
-    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc, int t,
-                                               int nblk, float (&acc)[4]) {
+    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
+                                               const uint8_t *, int t, int, int nblk, float (&acc)[4]) {
 #pragma unroll 8
         for (int c = 0; c < 8; ++c) {
             if (c >= nblk) break;
@@ -117,8 +110,8 @@ template <> struct Step<VKF_DEQUANT_Q4_0> {
 };
 
 template <> struct Step<VKF_DEQUANT_Q8_0> {
-    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc, int t,
-                                               int nblk, float (&acc)[4]) {
+    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
+                                               const uint8_t *, int t, int, int nblk, float (&acc)[4]) {
 #pragma unroll 8
         for (int c = 0; c < 8; ++c) {
             if (c >= nblk) break;
@@ -167,18 +160,23 @@ struct KScales {
 };
 
 // Q4_K and Q5_K (dequant_q4_k.glsl / dequant_q5_k.glsl): value = (d*sc)*q - dmin*m.
-// A operand = sc*q (exact); a second MMA with A = m accumulates sum m*x.
-template <bool Q5> struct StepK {
-    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc, int t,
-                                               float (&acc)[4]) {
+// A operand = sc*q (exact).  The min term sum_j m_j * X_j, X_j the sum of
+// the activations over sub-block j, is one extra MMA per super-block whose
+// k-slots are the 8 sub-blocks: A = m_j, B = X_j split into fp16 hi (slots
+// 0..7) + lo (slots 8..15), precomputed once per CTA.  Each call decodes one
+// 128-value half (PART) of the super-block; PART 0 also does the min MMA.
+template <bool Q5, int PART> struct StepK {
+    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
+                                               const uint8_t *xs, int t, float (&acc)[4]) {
         constexpr int QS = Q5 ? 48 : 16;
-        float da = hbits(ra), dma = hbits(ra + 2), db = hbits(rb), dmb = hbits(rb + 2);
+        const float da = hbits(ra), db = hbits(rb);
         KScales ka(ra + 4), kb(rb + 4);
-        float p1[4], p2[4];
-        zero4(p1);
-        zero4(p2);
+        float p1[2][4];
+        zero4(p1[0]);
+        zero4(p1[1]);
 #pragma unroll
-        for (int il = 0; il < 4; ++il) {
+        for (int i = 0; i < 2; ++i) {
+            const int il = 2 * PART + i;
             const int j0 = 2 * il, j1 = 2 * il + 1;
             uint32_t sla = ka.sc(j0), slb = kb.sc(j0);
             uint32_t cla = hmul2_u(sla, H2_M1024), clb = hmul2_u(slb, H2_M1024);
@@ -186,11 +184,6 @@ template <bool Q5> struct StepK {
             uint32_t cha = hmul2_u(sha, H2_M64), chb = hmul2_u(shb, H2_M64);
             sha = hmul2_u(sha, H2_SIXTEENTH);
             shb = hmul2_u(shb, H2_SIXTEENTH);
-            uint32_t am0[4], am1[4];
-            am0[0] = am0[2] = ka.mn(j0);
-            am0[1] = am0[3] = kb.mn(j0);
-            am1[0] = am1[2] = ka.mn(j1);
-            am1[1] = am1[3] = kb.mn(j1);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 uint32_t wa = ld32(ra + QS + 32 * il + 16 * h + 4 * t);
@@ -202,7 +195,7 @@ template <bool Q5> struct StepK {
                 uint32_t hb0 = lop3_and_or(wb, 0x00F000F0u, H2_MAGIC), hb1 = lop3_and_or(wb8, 0x00F000F0u, H2_MAGIC);
                 if constexpr (Q5) {
                     // 5th bit: qh[l] bit j0 (low nibbles) / j1 (high nibbles), dequant_q5_k.glsl:57-69
-                    uint32_t qa = ld32(ra + 16 + 16 * h + 4 * t), qb = ld32(rb + 16 + 16 * h + 4 * t);
+                    const uint32_t qa = ld32(ra + 16 + 16 * h + 4 * t), qb = ld32(rb + 16 + 16 * h + 4 * t);
                     auto lo02 = [&](uint32_t q) { return j0 <= 4 ? (q << (4 - j0)) : (q >> (j0 - 4)); };
                     la0 = lop3_and_or(lo02(qa), 0x00100010u, la0);
                     lb0 = lop3_and_or(lo02(qb), 0x00100010u, lb0);
@@ -213,88 +206,107 @@ template <bool Q5> struct StepK {
                     ha1 = lop3_and_or(qa >> j1, 0x01000100u, ha1);
                     hb1 = lop3_and_or(qb >> j1, 0x01000100u, hb1);
                 }
-                uint32_t alo[4] = {hfma2_u(la0, sla, cla), hfma2_u(lb0, slb, clb), hfma2_u(la1, sla, cla),
-                                   hfma2_u(lb1, slb, clb)};
-                uint32_t ahi[4] = {hfma2_u(ha0, sha, cha), hfma2_u(hb0, shb, chb), hfma2_u(ha1, sha, cha),
-                                   hfma2_u(hb1, shb, chb)};
+                const uint32_t alo[4] = {hfma2_u(la0, sla, cla), hfma2_u(lb0, slb, clb), hfma2_u(la1, sla, cla),
+                                         hfma2_u(lb1, slb, clb)};
+                const uint32_t ahi[4] = {hfma2_u(ha0, sha, cha), hfma2_u(hb0, shb, chb), hfma2_u(ha1, sha, cha),
+                                         hfma2_u(hb1, shb, chb)};
                 uint32_t b0, b1, b2, b3;
                 xfrag(xc, 64 * il + 16 * h, t, b0, b1);
                 xfrag(xc, 64 * il + 32 + 16 * h, t, b2, b3);
-                mma_16816(p1, alo, b0, b1, p1);
-                mma_16816(p1, ahi, b2, b3, p1);
-                mma_16816(p2, am0, b0, b1, p2);
-                mma_16816(p2, am1, b2, b3, p2);
+                mma_16816(p1[h], alo, b0, b1, p1[h]);
+                mma_16816(p1[h], ahi, b2, b3, p1[h]);
             }
         }
-        acc[0] = fmaf(-dma, p2[0], fmaf(da, p1[0], acc[0]));
-        acc[1] = fmaf(-dma, p2[1], fmaf(da, p1[1], acc[1]));
-        acc[2] = fmaf(-dmb, p2[2], fmaf(db, p1[2], acc[2]));
-        acc[3] = fmaf(-dmb, p2[3], fmaf(db, p1[3], acc[3]));
+        float p2[4];
+        zero4(p2);
+        if constexpr (PART == 0) {
+            // thread t holds sub-blocks 2t, 2t+1: A = (m, m) for rows g, g+8; B = sums (hi | lo)
+            const uint32_t sel = (t & 1) ? 0x4342u : 0x4140u;
+            uint32_t am[4];
+            am[0] = am[2] = hsub2_u(prmt(t < 2 ? ka.mA : ka.mB, 0x64646464u, sel), H2_1024);
+            am[1] = am[3] = hsub2_u(prmt(t < 2 ? kb.mA : kb.mB, 0x64646464u, sel), H2_1024);
+            const uint2 v = *reinterpret_cast<const uint2 *>(xs + 8 * t);
+            mma_16816(p2, am, v.x, v.y, p2);
+        }
+        const float dma = PART == 0 ? hbits(ra + 2) : 0.f, dmb = PART == 0 ? hbits(rb + 2) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float d = i < 2 ? da : db, dm = i < 2 ? dma : dmb;
+            acc[i] = fmaf(-dm, p2[i], fmaf(d, p1[0][i] + p1[1][i], acc[i]));
+        }
     }
 };
 
 template <> struct Step<VKF_DEQUANT_Q4_K> {
-    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc, int t,
-                                               int, float (&acc)[4]) {
-        StepK<false>::run(ra, rb, xc, t, acc);
+    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
+                                               const uint8_t *xs, int t, int part, int, float (&acc)[4]) {
+        if (part) StepK<false, 1>::run(ra, rb, xc, xs, t, acc);
+        else StepK<false, 0>::run(ra, rb, xc, xs, t, acc);
     }
 };
 template <> struct Step<VKF_DEQUANT_Q5_K> {
-    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc, int t,
-                                               int, float (&acc)[4]) {
-        StepK<true>::run(ra, rb, xc, t, acc);
+    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
+                                               const uint8_t *xs, int t, int part, int, float (&acc)[4]) {
+        if (part) StepK<true, 1>::run(ra, rb, xc, xs, t, acc);
+        else StepK<true, 0>::run(ra, rb, xc, xs, t, acc);
     }
 };
 
 // Q6_K (dequant_q6_k.glsl:28-58): value = d * sc16 * (q6 - 32), one int8 scale
-// per 16 values; A operand = q6 - 32 (exact), each MMA's partial scaled by d*sc.
-template <> struct Step<VKF_DEQUANT_Q6_K> {
+// per 16 values; A operand = q6 - 32 (exact), each MMA's partial scaled by
+// d*sc in fp32.  PART = ip selects the 128-value half.
+template <int IP> struct StepQ6 {
     __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc, int t,
-                                               int, float (&acc)[4]) {
-        float da = hbits(ra + 208), db = hbits(rb + 208);
+                                               float (&acc)[4]) {
+        const float da = hbits(ra + 208), db = hbits(rb + 208);
         const int8_t *sa = reinterpret_cast<const int8_t *>(ra + 192);
         const int8_t *sb = reinterpret_cast<const int8_t *>(rb + 192);
 #pragma unroll
-        for (int ip = 0; ip < 2; ++ip) {
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t qha = ld_u32_a2(ra + 128 + 32 * IP + 16 * h + 4 * t);
+            const uint32_t qhb = ld_u32_a2(rb + 128 + 32 * IP + 16 * h + 4 * t);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                uint32_t qha = ld_u32_a2(ra + 128 + 32 * ip + 16 * h + 4 * t);
-                uint32_t qhb = ld_u32_a2(rb + 128 + 32 * ip + 16 * h + 4 * t);
+            for (int half = 0; half < 2; ++half) {  // ql bytes at +0 / +32 (s & 1)
+                const uint32_t qla = ld_u32_a2(ra + 64 * IP + 32 * half + 16 * h + 4 * t);
+                const uint32_t qlb = ld_u32_a2(rb + 64 * IP + 32 * half + 16 * h + 4 * t);
+                const uint32_t qla8 = qla >> 8, qlb8 = qlb >> 8;
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {  // ql bytes at +0 / +32 (s&1)
-                    uint32_t qla = ld_u32_a2(ra + 64 * ip + 32 * half + 16 * h + 4 * t);
-                    uint32_t qlb = ld_u32_a2(rb + 64 * ip + 32 * half + 16 * h + 4 * t);
-                    uint32_t qla8 = qla >> 8, qlb8 = qlb >> 8;
-#pragma unroll
-                    for (int hiN = 0; hiN < 2; ++hiN) {
-                        const int s = half + 2 * hiN;
-                        uint32_t a[4];
-                        if (hiN == 0) {
-                            a[0] = hsub2_u(lop3_and_or(qha << (4 - 2 * s), 0x00300030u, lop3_and_or(qla, 0x000F000Fu, H2_MAGIC)), H2_1056);
-                            a[1] = hsub2_u(lop3_and_or(qhb << (4 - 2 * s), 0x00300030u, lop3_and_or(qlb, 0x000F000Fu, H2_MAGIC)), H2_1056);
-                            a[2] = hsub2_u(lop3_and_or(qha >> (4 + 2 * s), 0x00300030u, lop3_and_or(qla8, 0x000F000Fu, H2_MAGIC)), H2_1056);
-                            a[3] = hsub2_u(lop3_and_or(qhb >> (4 + 2 * s), 0x00300030u, lop3_and_or(qlb8, 0x000F000Fu, H2_MAGIC)), H2_1056);
-                        } else {
-                            a[0] = hfma2_u(lop3_and_or(qha << (8 - 2 * s), 0x03000300u, lop3_and_or(qla, 0x00F000F0u, H2_MAGIC)), H2_SIXTEENTH, H2_M96);
-                            a[1] = hfma2_u(lop3_and_or(qhb << (8 - 2 * s), 0x03000300u, lop3_and_or(qlb, 0x00F000F0u, H2_MAGIC)), H2_SIXTEENTH, H2_M96);
-                            a[2] = hfma2_u(lop3_and_or(qha >> (2 * s), 0x03000300u, lop3_and_or(qla8, 0x00F000F0u, H2_MAGIC)), H2_SIXTEENTH, H2_M96);
-                            a[3] = hfma2_u(lop3_and_or(qhb >> (2 * s), 0x03000300u, lop3_and_or(qlb8, 0x00F000F0u, H2_MAGIC)), H2_SIXTEENTH, H2_M96);
-                        }
-                        uint32_t b0, b1;
-                        xfrag(xc, 128 * ip + 32 * s + 16 * h, t, b0, b1);
-                        float p[4];
-                        zero4(p);
-                        mma_16816(p, a, b0, b1, p);
-                        const int is = 8 * ip + 2 * s + h;
-                        float fa = da * (float)sa[is], fb = db * (float)sb[is];
-                        acc[0] = fmaf(fa, p[0], acc[0]);
-                        acc[1] = fmaf(fa, p[1], acc[1]);
-                        acc[2] = fmaf(fb, p[2], acc[2]);
-                        acc[3] = fmaf(fb, p[3], acc[3]);
+                for (int hiN = 0; hiN < 2; ++hiN) {
+                    const int s = half + 2 * hiN;
+                    uint32_t a[4];
+                    if (hiN == 0) {
+                        a[0] = hsub2_u(lop3_and_or(qha << (4 - 2 * s), 0x00300030u, lop3_and_or(qla, 0x000F000Fu, H2_MAGIC)), H2_1056);
+                        a[1] = hsub2_u(lop3_and_or(qhb << (4 - 2 * s), 0x00300030u, lop3_and_or(qlb, 0x000F000Fu, H2_MAGIC)), H2_1056);
+                        a[2] = hsub2_u(lop3_and_or(qha >> (4 + 2 * s), 0x00300030u, lop3_and_or(qla8, 0x000F000Fu, H2_MAGIC)), H2_1056);
+                        a[3] = hsub2_u(lop3_and_or(qhb >> (4 + 2 * s), 0x00300030u, lop3_and_or(qlb8, 0x000F000Fu, H2_MAGIC)), H2_1056);
+                    } else {
+                        a[0] = hfma2_u(lop3_and_or(qha << (8 - 2 * s), 0x03000300u, lop3_and_or(qla, 0x00F000F0u, H2_MAGIC)), H2_SIXTEENTH, H2_M96);
+                        a[1] = hfma2_u(lop3_and_or(qhb << (8 - 2 * s), 0x03000300u, lop3_and_or(qlb, 0x00F000F0u, H2_MAGIC)), H2_SIXTEENTH, H2_M96);
+                        a[2] = hfma2_u(lop3_and_or(qha >> (2 * s), 0x03000300u, lop3_and_or(qla8, 0x00F000F0u, H2_MAGIC)), H2_SIXTEENTH, H2_M96);
+                        a[3] = hfma2_u(lop3_and_or(qhb >> (2 * s), 0x03000300u, lop3_and_or(qlb8, 0x00F000F0u, H2_MAGIC)), H2_SIXTEENTH, H2_M96);
                     }
+                    uint32_t b0, b1;
+                    xfrag(xc, 128 * IP + 32 * s + 16 * h, t, b0, b1);
+                    float p[4];
+                    zero4(p);
+                    mma_16816(p, a, b0, b1, p);
+                    const int is = 8 * IP + 2 * s + h;
+                    const float fa = da * (float)sa[is], fb = db * (float)sb[is];
+                    acc[0] = fmaf(fa, p[0], acc[0]);
+                    acc[1] = fmaf(fa, p[1], acc[1]);
+                    acc[2] = fmaf(fb, p[2], acc[2]);
+                    acc[3] = fmaf(fb, p[3], acc[3]);
                 }
             }
         }
+    }
+};
+
+template <> struct Step<VKF_DEQUANT_Q6_K> {
+    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
+                                               const uint8_t *, int t, int part, int, float (&acc)[4]) {
+        if (part) StepQ6<1>::run(ra, rb, xc, t, acc);
+        else StepQ6<0>::run(ra, rb, xc, t, acc);
     }
 };
 

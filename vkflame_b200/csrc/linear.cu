@@ -11,8 +11,10 @@
 
 namespace vkf {
 int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void *Y, int y_f16, int64_t ldy, int M,
-                int N, int K, cudaStream_t stream, void *scratch, size_t scratch_cap);
-size_t gemv_scratch_bytes(int N, int sms, int occ);
+                int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap);
+size_t gemv_ws_floats(int sms);
+size_t gemv_counters(int N);
+int gemv_cols_per_launch(int K);
 int q8_1_to_f16(const void *src, void *dst, int M, int K, int64_t ldb, int64_t ldo, cudaStream_t stream);
 
 static bool gemv_format(int wtype) {
@@ -21,7 +23,7 @@ static bool gemv_format(int wtype) {
 }
 
 // Decode path for M <= 8 (and, until the tensor-core GEMM covers a format,
-// for larger M in chunks of 8 rows).
+// for larger M in column groups).
 static int quant_linear_gemv(const void *W, int wtype, const void *X, int xtype, void *Y, int ytype, int M, int N,
                              int K, int64_t ldx, int64_t ldy, cudaStream_t stream) {
     DeviceState *ds = device_state();
@@ -31,9 +33,11 @@ static int quant_linear_gemv(const void *W, int wtype, const void *X, int xtype,
     const bool direct = xtype == VKF_X_F16 && ((uintptr_t)X & 15) == 0 && (ldx * 2) % 16 == 0;
     const int64_t ldx_st = ((int64_t)K * 2 + 15) / 16 * 16;  // staged row stride, bytes
     const size_t stage_bytes = direct ? 0 : (((size_t)M * ldx_st + 255) & ~size_t(255));
-    const size_t gemv_bytes = gemv_scratch_bytes(N, ds->sm_count, 4);
-    uint8_t *scr = (uint8_t *)stream_scratch(stream, stage_bytes + gemv_bytes);
-    if (!scr) return VKF_ERR_NOMEM;
+    const size_t ws_floats = gemv_ws_floats(ds->sm_count);
+    uint8_t *scr = (uint8_t *)stream_scratch(stream, stage_bytes + ws_floats * sizeof(float));
+    const size_t ncnt = gemv_counters(N);
+    int *cnt = stream_counters(stream, ncnt);
+    if (!scr || !cnt) return VKF_ERR_NOMEM;
     const void *xf = X;
     int64_t ldx_bytes = ldx * 2;
     if (!direct) {
@@ -49,11 +53,15 @@ static int quant_linear_gemv(const void *W, int wtype, const void *X, int xtype,
         ldx_bytes = ldx_st;
     }
     const int y_f16 = ytype == VKF_Y_F16;
-    for (int m0 = 0; m0 < M; m0 += 8) {
-        const int mc = M - m0 < 8 ? M - m0 : 8;
+    // Batch columns are processed in groups whose activations fit the
+    // kernel's resident shared-memory budget (all 8 when K <= 4608).
+    const int cols = gemv_cols_per_launch(K);
+    for (int m0 = 0; m0 < M; m0 += cols) {
+        const int mc = M - m0 < cols ? M - m0 : cols;
         const void *xm = (const uint8_t *)xf + m0 * ldx_bytes;
         void *ym = (uint8_t *)Y + (size_t)m0 * ldy * (y_f16 ? 2 : 4);
-        int rc = gemv_launch(wtype, W, xm, ldx_bytes, ym, y_f16, ldy, mc, N, K, stream, scr + stage_bytes, gemv_bytes);
+        int rc = gemv_launch(wtype, W, xm, ldx_bytes, ym, y_f16, ldy, mc, N, K, stream,
+                             reinterpret_cast<float *>(scr + stage_bytes), ws_floats, cnt, ncnt);
         if (rc) return rc;
     }
     return VKF_OK;

@@ -27,6 +27,10 @@ DeviceState *device_state();  // current device; nullptr if CUDA has no device
 // per-stream arena is never used by two kernels at once.  Growing waits for
 // the stream first.  Returns nullptr on allocation failure.
 void *stream_scratch(cudaStream_t stream, size_t bytes);
+// Arrival counters for one stream on the current device: a separate, zeroed
+// allocation that kernels leave zeroed again when they finish (so nothing
+// else may write it).  Returns nullptr on allocation failure.
+int *stream_counters(cudaStream_t stream, size_t count);
 
 // Checks the launch just made; maps failures to VKF_ERR_CUDA.
 int check_launch();
@@ -42,3 +46,4 @@ void log(const char *fmt, ...);
 
 // Kernel error bits written to DeviceState::d_error.
 #define VKF_KERR_WAIT_TIMEOUT 1u
+#define VKF_KERR_BAD_COPY 2u

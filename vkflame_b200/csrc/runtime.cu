@@ -101,13 +101,13 @@ struct Arena {
     size_t size = 0;
 };
 static std::mutex g_scratch_mu;
-static std::map<std::pair<int, cudaStream_t>, Arena> g_scratch;
+static std::map<std::pair<int, cudaStream_t>, Arena> g_scratch, g_counters;
 
-void *stream_scratch(cudaStream_t stream, size_t bytes) {
+static void *arena_get(std::map<std::pair<int, cudaStream_t>, Arena> &tab, cudaStream_t stream, size_t bytes) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
     std::lock_guard<std::mutex> lk(g_scratch_mu);
-    Arena &a = g_scratch[{dev, stream}];
+    Arena &a = tab[{dev, stream}];
     if (a.size >= bytes) return a.ptr;
     size_t want = bytes < (size_t(4) << 20) ? (size_t(4) << 20) : bytes;
     want = (want + 0xFFFFF) & ~size_t(0xFFFFF);
@@ -125,8 +125,14 @@ void *stream_scratch(cudaStream_t stream, size_t bytes) {
     }
     a.ptr = p;
     a.size = want;
-    log("scratch for stream %p on device %d: %zu bytes\n", (void *)stream, dev, want);
+    log("arena for stream %p on device %d: %zu bytes\n", (void *)stream, dev, want);
     return p;
+}
+
+void *stream_scratch(cudaStream_t stream, size_t bytes) { return arena_get(g_scratch, stream, bytes); }
+
+int *stream_counters(cudaStream_t stream, size_t count) {
+    return (int *)arena_get(g_counters, stream, count * sizeof(int));
 }
 
 // ---- allocation table ------------------------------------------------------
@@ -191,7 +197,8 @@ void *vkflame_get_context(void) {
 
 void vkflame_shutdown(void) {
     std::lock_guard<std::mutex> lk(g_scratch_mu);
-    for (auto &kv : g_scratch) {
+    for (auto *tab : {&g_scratch, &g_counters})
+    for (auto &kv : *tab) {
         int cur = 0;
         cudaGetDevice(&cur);
         cudaSetDevice(kv.first.first);
@@ -200,6 +207,7 @@ void vkflame_shutdown(void) {
         cudaSetDevice(cur);
     }
     g_scratch.clear();
+    g_counters.clear();
 }
 
 void vkflame_print_info(void) {
