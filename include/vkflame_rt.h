@@ -107,6 +107,15 @@ int vkflame_dispatch_dequant_async(const void *src, void *dst, uint64_t n_blocks
 int vkflame_quant_linear(const void *W, int wtype, const void *X, int xtype, void *Y, int ytype,
                          int M, int N, int K, int64_t ldx, int64_t ldy, void *stream);
 
+/* vkflame_quant_linear with flags.  VKF_FLAG_STATIC_WEIGHTS: W is not
+ * written by the kernel launched just before this call on the same stream
+ * (true of model weights), so the kernel may start streaming W while that
+ * kernel is still running.  Without the flag all of this call's memory
+ * accesses wait for the preceding kernel. */
+#define VKF_FLAG_STATIC_WEIGHTS 1u
+int vkflame_quant_linear_ex(const void *W, int wtype, const void *X, int xtype, void *Y, int ytype,
+                            int M, int N, int K, int64_t ldx, int64_t ldy, unsigned flags, void *stream);
+
 /* On-device fp32 -> Q8_1 quantiser (no reference counterpart: the reference
  * only decodes Q8_1, kernels/dequant_q8_1.glsl).  x is M x K fp32 (row stride
  * ldx elements), y receives M rows of K/32 blocks (36 B each), packed.

@@ -93,14 +93,13 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 // a[2] = (row g, k 2t+8..), a[3] = (row g+8, k 2t+8..); B (16x8): b[0] = (k 2t.., col g),
 // b[1] = (k 2t+8.., col g); C: c[0..1] = (row g, col 2t..2t+1), c[2..3] = (row g+8, ...).
 // g = lane >> 2, t = lane & 3.
-__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
-                                          const float (&c)[4]) {
+// Accumulates in place (d += A*B): read-write operands avoid register copies.
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%11,%12,%13};"
-        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
-          "f"(c[3]));
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t orv) {

@@ -15,21 +15,24 @@
 //
 //   warp CW       producer: one TMA bulk copy per row per item into an
 //                 NST-deep ring, completion by mbarrier transaction bytes.
-//   warps 0..CW-1 consumers: split the item's work units (256 values, or a
-//                 128-value half super-block for K-quants) between them,
-//                 decode into m16n8k16 fragments (gemv_q.cuh: A = the 16
-//                 weight rows, N = the M <= 8 activation columns) and keep a
-//                 per-warp fp32 accumulator; at the end of a row block the CW
-//                 partials are reduced through shared memory.
+//   warps 0..CW-1 consumers: take the work units (one super-block, or eight
+//                 32-value blocks, of the 16 rows) round-robin, decode them
+//                 into m16n8k16 fragments (gemv_q.cuh: A = the 16 weight
+//                 rows, N = the M <= 8 activation columns) and keep a per-warp
+//                 fp32 accumulator; they never wait for each other, and the
+//                 last warp to finish a row block reduces the CW partials.
 //
 // The activations X (M x K fp16) stay resident in shared memory for the whole
 // CTA, stored permuted in fragment order; the fp32 sums of every 32-value
 // sub-block (hi + lo fp16) are precomputed next to them for the K-quant
 // min-term MMA.  Scheduling is stream-K over the (row block, K-range) items:
-// the iteration space is split evenly over one CTA per SM, and a row block
-// split between CTAs is finished by its last contributor, which sums the
+// the iteration space is split evenly over one or two CTAs per SM, a row block
+// split between CTAs being finished by its last contributor, which sums the
 // partials in CTA order (deterministic) from scratch memory.  Batch columns
 // that do not fit the resident budget are processed in groups by the caller.
+// Launches use programmatic dependent launch (griddepcontrol): a launch's
+// prologue, and with static weights its weight streaming, overlaps the tail
+// of the previous kernel on the stream.
 
 #include "gemv_q.cuh"
 
@@ -39,12 +42,16 @@
 namespace vkf {
 namespace gemv {
 
-constexpr int CW = 16;                // consumer warps
+constexpr int CW = 8;                 // consumer warps
 constexpr int NT = 32 * (CW + 1);
 constexpr int NST = 3;                // ring depth
-constexpr int ROW_BUDGET = 3040;      // max bytes of one row per item
+constexpr int ROW_BUDGET = 1600;      // max bytes of one row per item
 constexpr int X_BUDGET = 80 * 1024;   // resident activations + sums
 constexpr int SMEM_MAX = 227 * 1024;
+// Two CTAs per SM when the activations are small: a CTA of the next launch
+// on the stream can then stream its weights while this one drains.
+constexpr int SMEM_HALF = 112 * 1024;
+constexpr int X_HALF = 36 * 1024;
 constexpr int ZERO_BYTES = 1024;      // zero activations / sums for columns >= M
 
 struct Args {
@@ -67,6 +74,9 @@ struct Args {
     int *cnt;          // per-row-block arrival counters (zero between launches)
     unsigned *err;
     int y_f16;
+    int prefetch;      // stream weights before the previous kernel on the stream completes
+    int probe;         // debug (VKFLAME_GEMV_PROBE): 1 skips the decode (data path alone), 2 skips the
+                       // copies and waits (decode alone, on whatever the ring holds)
 };
 
 __device__ __forceinline__ int cta_of(int64_t i, const Args &a) { return (int)(((i + 1) * a.G - 1) / a.I); }
@@ -81,7 +91,7 @@ __device__ __forceinline__ void store_y(const Args &a, int m, int n, float v) {
 }
 
 template <int QT>
-__global__ void __launch_bounds__(NT, 1) gemv_kernel(const __grid_constant__ Args a) {
+__global__ void __launch_bounds__(NT, 2) gemv_kernel(const __grid_constant__ Args a) {
     constexpr int QK = Fmt<QT>::QK, BB = Fmt<QT>::BB, PARTS = Fmt<QT>::PARTS;
     constexpr int UB = (256 / QK) * BB;  // bytes of one 256-value unit of a row
     constexpr bool KQ = QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K;  // has a min term
@@ -92,11 +102,16 @@ __global__ void __launch_bounds__(NT, 1) gemv_kernel(const __grid_constant__ Arg
     uint8_t *ring = zero + ZERO_BYTES;                        // NST x stage_bytes
     uint64_t *full = reinterpret_cast<uint64_t *>(ring + NST * a.stage_bytes);
     uint64_t *empty = full + NST;
-    float *red = reinterpret_cast<float *>(empty + NST + 2);  // CW x 32 x 4
+    int *redcnt = reinterpret_cast<int *>(empty + NST);       // NST + 1 arrival counters
+    float *red = reinterpret_cast<float *>(empty + NST + 2);  // (NST + 1) x CW x 32 x 4
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cta = blockIdx.x;
     const int64_t it0 = first_iter(cta, a), it1 = first_iter(cta + 1, a);
+    // Programmatic dependent launch: let the next kernel on the stream start
+    // its prologue now; everything this kernel reads or writes that another
+    // kernel may touch (X, Y, the scratch) waits for the previous kernel.
+    asm volatile("griddepcontrol.launch_dependents;");
 
     for (int i = threadIdx.x; i < ZERO_BYTES / 16; i += NT) reinterpret_cast<uint4 *>(zero)[i] = make_uint4(0, 0, 0, 0);
     if (threadIdx.x == 0) {
@@ -104,12 +119,17 @@ __global__ void __launch_bounds__(NT, 1) gemv_kernel(const __grid_constant__ Arg
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], CW);
         }
+        for (int r = 0; r <= NST; ++r) redcnt[r] = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
     if (warp == CW) {
         // ---------------- producer ----------------
+        // Weights that no kernel writes (a.prefetch) are streamed at once;
+        // otherwise the producer too waits for the previous kernel.
+        if (!a.prefetch) asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (a.probe >= 2) return;
         int n = 0;
         for (int64_t it = it0; it < it1; ++it, ++n) {
             const int s = n % NST;
@@ -143,14 +163,32 @@ __global__ void __launch_bounds__(NT, 1) gemv_kernel(const __grid_constant__ Arg
     }
 
     // ---------------- consumers ----------------
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // Resident activations, permuted (x0, x2, x1, x3) per group of four.
+    // Loads are batched through registers (read-only path) so their
+    // latencies overlap instead of serialising behind the shared stores.
     {
-        const int groups = a.K / 4;
-        for (int i = threadIdx.x; i < a.M * groups; i += CW * 32) {
-            const int m = i / groups, q = i - m * groups;
-            const uint2 v = *reinterpret_cast<const uint2 *>(a.X + (int64_t)m * a.ldx_bytes + q * 8);
-            *reinterpret_cast<uint2 *>(xs + m * a.xpr + q * 8) =
-                make_uint2(prmt(v.x, v.y, 0x5410), prmt(v.x, v.y, 0x7632));
+        const int groups = a.K / 4, total = a.M * groups;
+        constexpr int B = 8;
+        for (int i0 = threadIdx.x; i0 < total; i0 += B * CW * 32) {
+            uint2 v[B];
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+                const int i = i0 + b * CW * 32;
+                if (i < total) {
+                    const int m = i / groups, q = i - m * groups;
+                    v[b] = __ldg(reinterpret_cast<const uint2 *>(a.X + (int64_t)m * a.ldx_bytes) + q);
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+                const int i = i0 + b * CW * 32;
+                if (i < total) {
+                    const int m = i / groups, q = i - m * groups;
+                    *reinterpret_cast<uint2 *>(xs + m * a.xpr + q * 8) =
+                        make_uint2(prmt(v[b].x, v[b].y, 0x5410), prmt(v[b].x, v[b].y, 0x7632));
+                }
+            }
         }
     }
     consumer_bar();
@@ -160,10 +198,21 @@ __global__ void __launch_bounds__(NT, 1) gemv_kernel(const __grid_constant__ Arg
         const int nsub = a.K / 32;
         for (int i = threadIdx.x; i < a.M * nsub; i += CW * 32) {
             const int m = i / nsub, j = i - m * nsub;
-            const __half *xr = reinterpret_cast<const __half *>(xs + m * a.xpr) + j * 32;
-            float sum = 0.f;
-#pragma unroll 8
-            for (int k = 0; k < 32; ++k) sum += __half2float(xr[k]);
+            const uint4 *xr = reinterpret_cast<const uint4 *>(xs + m * a.xpr + j * 64);
+            float part[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint4 v = xr[c];
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                float s2 = 0.f;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[e]));
+                    s2 += f.x + f.y;
+                }
+                part[c] = s2;
+            }
+            const float sum = (part[0] + part[1]) + (part[2] + part[3]);
             const __half hi = __float2half_rn(sum);
             const __half lo = __float2half_rn(sum - __half2float(hi));
             __half *o = reinterpret_cast<__half *>(sums + m * a.xsp + (j / 8) * 32 + ((j % 8) / 2) * 8) + (j & 1);
@@ -183,87 +232,101 @@ __global__ void __launch_bounds__(NT, 1) gemv_kernel(const __grid_constant__ Arg
     float acc[4];
     zero4(acc);
     const int first_tile = (int)(it0 / a.S);
+    // Warps take the units of the CTA's item sequence round-robin (unit i of
+    // the sequence goes to warp i mod CW), never waiting for each other: a
+    // warp releases a ring slot when done with it, and at the end of a row
+    // block leaves its partial in one of NST + 1 reduction buffers (a warp
+    // can run at most NST items ahead); the last warp to arrive reduces.
+    int ubase = 0;  // units of this CTA's earlier items, mod CW
+    int tiles_done = 0;
     int n = 0;
     for (int64_t it = it0; it < it1; ++it, ++n) {
         const int s = n % NST;
         const uint32_t ph = (uint32_t)(n / NST) & 1u;
-        if (ok) ok = mbar_wait(&full[s], ph, a.err);
+        if (ok && a.probe < 2) ok = mbar_wait(&full[s], ph, a.err);
         const int tile = (int)(it / a.S), step = (int)(it - (int64_t)tile * a.S);
         const int u0 = step * a.upi, nu = min(a.upi, a.units - u0);
-        if (ok) {
+        if (ok && (a.probe == 0 || a.probe == 2)) {
             const uint8_t *st = ring + s * a.stage_bytes;
             const int64_t row_a = (int64_t)tile * 16 + g, row_b = row_a + 8;
             const uintptr_t ga = (uintptr_t)a.W + row_a * a.row_bytes + (int64_t)u0 * UB;
             const uintptr_t gb = (uintptr_t)a.W + row_b * a.row_bytes + (int64_t)u0 * UB;
             const uint8_t *ra = st + g * a.rpb + (ga & 15), *rb = st + (g + 8) * a.rpb + (gb & 15);
-            for (int wi = warp; wi < nu * PARTS; wi += CW) {
-                const int u = wi / PARTS, part = wi - u * PARTS;
+            int u = warp - ubase;
+            if (u < 0) u += CW;
+            for (; u < nu; u += CW) {
                 const int kv = (u0 + u) * 256;
                 const int nblk = min(8, (a.K - kv) / 32);
                 const uint8_t *xc = xg ? xg + kv * 2 : zero;
                 const uint8_t *xsum = sg ? sg + (u0 + u) * 32 : zero;
-                Step<QT>::run(ra + u * UB, rb + u * UB, xc, xsum, t, part, nblk, acc);
+                Step<QT>::run(ra + u * UB, rb + u * UB, xc, xsum, t, 0, nblk, acc);
             }
         }
+        ubase = (ubase + nu) % CW;
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
 
         if (step != a.S - 1 && it + 1 != it1) continue;
 
-        // ---- row-block epilogue: reduce the CW warp partials ----
-        reinterpret_cast<float4 *>(red)[warp * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        consumer_bar();
-        if (warp == 0) {
-            float o[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int w = 0; w < CW; ++w) {
-                const float4 v = reinterpret_cast<const float4 *>(red)[w * 32 + lane];
-                o[0] += v.x;
-                o[1] += v.y;
-                o[2] += v.z;
-                o[3] += v.w;
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[i] = o[i];
+        // ---- row-block epilogue: the last warp to arrive reduces ----
+        const int rbuf = tiles_done % (NST + 1);
+        ++tiles_done;
+        float *rbase = red + rbuf * CW * 128;
+        reinterpret_cast<float4 *>(rbase)[warp * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        zero4(acc);
+        __threadfence_block();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&redcnt[rbuf], 1) == CW - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence_block();
+        float o[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int w = 0; w < CW; ++w) {
+            const float4 v = reinterpret_cast<const float4 *>(rbase)[w * 32 + lane];
+            o[0] += v.x;
+            o[1] += v.y;
+            o[2] += v.z;
+            o[3] += v.w;
         }
+        __syncwarp();
+        if (lane == 0) redcnt[rbuf] = 0;
         const int64_t tb = (int64_t)tile * a.S;
         const bool whole = tb >= it0 && tb + a.S <= it1;
-        bool write = warp == 0;
-        if (!whole && warp == 0) {
+        bool write = true;
+        if (!whole) {
             const int slot = tile == first_tile ? 0 : 1;
-            reinterpret_cast<float4 *>(a.ws + ((int64_t)cta * 2 + slot) * 128)[lane] =
-                make_float4(acc[0], acc[1], acc[2], acc[3]);
+            reinterpret_cast<float4 *>(a.ws + ((int64_t)cta * 2 + slot) * 128)[lane] = make_float4(o[0], o[1], o[2], o[3]);
             __threadfence();
             __syncwarp();
             const int c_first = cta_of(tb, a), c_last = cta_of(tb + a.S - 1, a);
-            int last = 0;
-            if (lane == 0) last = atomicAdd(&a.cnt[tile], 1) == c_last - c_first;
-            last = __shfl_sync(0xffffffffu, last, 0);
-            write = last != 0;
+            int fin = 0;
+            if (lane == 0) fin = atomicAdd(&a.cnt[tile], 1) == c_last - c_first;
+            fin = __shfl_sync(0xffffffffu, fin, 0);
+            write = fin != 0;
             if (write) {
                 __threadfence();
-                zero4(acc);
+                zero4(o);
 #pragma unroll 4
                 for (int c = c_first; c <= c_last; ++c) {
                     const int cslot = (tile == (int)(first_iter(c, a) / a.S)) ? 0 : 1;
                     const float4 v =
                         __ldcg(reinterpret_cast<const float4 *>(a.ws + ((int64_t)c * 2 + cslot) * 128) + lane);
-                    acc[0] += v.x;
-                    acc[1] += v.y;
-                    acc[2] += v.z;
-                    acc[3] += v.w;
+                    o[0] += v.x;
+                    o[1] += v.y;
+                    o[2] += v.z;
+                    o[3] += v.w;
                 }
                 if (lane == 0) atomicExch(&a.cnt[tile], 0);
             }
         }
         if (write) {
             const int row = tile * 16 + g;
-            store_y(a, 2 * t, row, acc[0]);
-            store_y(a, 2 * t + 1, row, acc[1]);
-            store_y(a, 2 * t, row + 8, acc[2]);
-            store_y(a, 2 * t + 1, row + 8, acc[3]);
+            store_y(a, 2 * t, row, o[0]);
+            store_y(a, 2 * t + 1, row, o[1]);
+            store_y(a, 2 * t, row + 8, o[2]);
+            store_y(a, 2 * t + 1, row + 8, o[3]);
         }
-        zero4(acc);
-        consumer_bar();  // `red` is reused by the next row block
     }
 }
 
@@ -276,8 +339,9 @@ struct Launcher {
         a.units = (a.K + 255) / 256;
         a.xpr = ((a.K * 2 + 95) / 128) * 128 + 32;  // pitch = 8 banks mod 32: conflict-free fragment loads
         a.xsp = KQ ? ((a.K / 256) * 32 + 15) / 16 * 16 : 0;
-        const int fixed = a.M * (a.xpr + a.xsp) + ZERO_BYTES + 2 * NST * 8 + 16 + CW * 32 * 16;
-        const int row_avail = (SMEM_MAX - fixed) / (NST * 16) - 32;  // room for padding and misalignment
+        const int fixed = a.M * (a.xpr + a.xsp) + ZERO_BYTES + 2 * NST * 8 + 16 + (NST + 1) * CW * 32 * 16;
+        const int budget = a.M * (a.xpr + a.xsp) <= X_HALF ? SMEM_HALF : SMEM_MAX;
+        const int row_avail = (budget - fixed) / (NST * 16) - 32;  // room for padding and misalignment
         const int umax = std::min(ROW_BUDGET, row_avail) / UB;
         if (umax < 1) return VKF_ERR_UNSUPPORTED;
         a.S = (a.units + umax - 1) / umax;
@@ -289,7 +353,7 @@ struct Launcher {
         a.rpb = ng * 16;
         a.stage_bytes = 16 * a.rpb;
         const size_t smem = (size_t)fixed + NST * (size_t)a.stage_bytes;
-        if (smem > SMEM_MAX) return VKF_ERR_UNSUPPORTED;
+        if (smem > (size_t)budget) return VKF_ERR_UNSUPPORTED;
         static bool attr_set[64] = {false};
         int dev = 0;
         cudaGetDevice(&dev);
@@ -297,11 +361,23 @@ struct Launcher {
             cudaFuncSetAttribute(gemv_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX);
             attr_set[dev] = true;
         }
-        a.G = (int)std::max<int64_t>(1, std::min<int64_t>(sms, a.I));
+        a.G = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)sms * (budget == SMEM_HALF ? 2 : 1), a.I));
         if ((size_t)a.G * 2 * 128 > ws_cap || (size_t)a.T > cnt_cap) return VKF_ERR_INVALID;
         a.ws = ws;
         a.cnt = cnt;
-        gemv_kernel<QT><<<a.G, NT, smem, stream>>>(a);
+        static const int probe = [] { const char *e = getenv("VKFLAME_GEMV_PROBE"); return e ? atoi(e) : 0; }();
+        a.probe = probe;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(a.G);
+        cfg.blockDim = dim3(NT);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaLaunchKernelEx(&cfg, gemv_kernel<QT>, a);
         return check_launch();
     }
 };
@@ -314,11 +390,11 @@ int gemv_cols_per_launch(int K) {
     return (int)std::max<size_t>(1, std::min<size_t>(8, gemv::X_BUDGET / per));
 }
 size_t gemv_counters(int N) { return (size_t)(N + 15) / 16; }
-size_t gemv_ws_floats(int sms) { return (size_t)sms * 2 * 128; }
+size_t gemv_ws_floats(int sms) { return (size_t)sms * 2 * 2 * 128; }
 
 // X: fp16, rows 16-byte aligned (ldx_bytes multiple of 16).  Checked by caller.
 int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void *Y, int y_f16, int64_t ldy, int M,
-                int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap) {
+                int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap, int prefetch) {
     DeviceState *ds = device_state();
     if (!ds) return VKF_ERR_NO_DEVICE;
     gemv::Args a{};
@@ -333,6 +409,7 @@ int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void
     a.row_bytes = (int64_t)K / vkf_qtype_block_values(wtype) * vkf_qtype_block_bytes(wtype);
     a.err = ds->d_error;
     a.y_f16 = y_f16;
+    a.prefetch = prefetch;
     const int sms = ds->sm_count;
     switch (wtype) {
     case VKF_DEQUANT_Q4_0: return gemv::Launcher<VKF_DEQUANT_Q4_0>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);

@@ -24,13 +24,14 @@
 namespace vkf {
 namespace gemv {
 
-// QK values per block, BB bytes per block, PARTS work units per 256 values.
+// QK values per block, BB bytes per block, PARTS work units per 256 values
+// (1: a warp decodes whole super-blocks / 8-block groups).
 template <int QT> struct Fmt;
 template <> struct Fmt<VKF_DEQUANT_Q4_0> { static constexpr int QK = 32, BB = 18, PARTS = 1; };
 template <> struct Fmt<VKF_DEQUANT_Q8_0> { static constexpr int QK = 32, BB = 34, PARTS = 1; };
-template <> struct Fmt<VKF_DEQUANT_Q4_K> { static constexpr int QK = 256, BB = 144, PARTS = 2; };
-template <> struct Fmt<VKF_DEQUANT_Q5_K> { static constexpr int QK = 256, BB = 176, PARTS = 2; };
-template <> struct Fmt<VKF_DEQUANT_Q6_K> { static constexpr int QK = 256, BB = 210, PARTS = 2; };
+template <> struct Fmt<VKF_DEQUANT_Q4_K> { static constexpr int QK = 256, BB = 144, PARTS = 1; };
+template <> struct Fmt<VKF_DEQUANT_Q5_K> { static constexpr int QK = 256, BB = 176, PARTS = 1; };
+template <> struct Fmt<VKF_DEQUANT_Q6_K> { static constexpr int QK = 256, BB = 210, PARTS = 1; };
 
 // fp16 constants (bit patterns)
 constexpr uint32_t H2_MAGIC = 0x64006400u;  // (1024, 1024)
@@ -71,7 +72,6 @@ __device__ __forceinline__ void zero4(float (&p)[4]) { p[0] = p[1] = p[2] = p[3]
 //           unit: one super-block, or eight 32-value blocks)
 //   xc:     permuted activations of column g at the unit's first value
 //   xs:     (Q4_K, Q5_K) sub-block sums of column g for this super-block
-//   part:   (K-quants) which 128-value half of the super-block
 //   nblk:   32-value blocks present (tail unit of Q4_0 / Q8_0)
 template <int QT> struct Step;
 
@@ -99,8 +99,8 @@ template <> struct Step<VKF_DEQUANT_Q4_0> {
             xfrag(xc, c * 32 + 16, t, b2, b3);
             float p[4];
             zero4(p);
-            mma_16816(p, alo, b0, b1, p);
-            mma_16816(p, ahi, b2, b3, p);
+            mma_16816(p, alo, b0, b1);
+            mma_16816(p, ahi, b2, b3);
             acc[0] = fmaf(da, p[0], acc[0]);
             acc[1] = fmaf(da, p[1], acc[1]);
             acc[2] = fmaf(db, p[2], acc[2]);
@@ -129,7 +129,7 @@ template <> struct Step<VKF_DEQUANT_Q8_0> {
                 a[3] = hsub2_u(lop3_and_xor(wb >> 8, 0x00FF00FFu, 0x64806480u), H2_1152);
                 uint32_t b0, b1;
                 xfrag(xc, c * 32 + 16 * h, t, b0, b1);
-                mma_16816(p, a, b0, b1, p);
+                mma_16816(p, a, b0, b1);
             }
             acc[0] = fmaf(da, p[0], acc[0]);
             acc[1] = fmaf(da, p[1], acc[1]);
@@ -163,9 +163,9 @@ struct KScales {
 // A operand = sc*q (exact).  The min term sum_j m_j * X_j, X_j the sum of
 // the activations over sub-block j, is one extra MMA per super-block whose
 // k-slots are the 8 sub-blocks: A = m_j, B = X_j split into fp16 hi (slots
-// 0..7) + lo (slots 8..15), precomputed once per CTA.  Each call decodes one
-// 128-value half (PART) of the super-block; PART 0 also does the min MMA.
-template <bool Q5, int PART> struct StepK {
+// 0..7) + lo (slots 8..15), precomputed once per CTA.  Each call decodes a
+// range of 64-value chunks [IL0, IL0 + NIL); IL0 == 0 also does the min MMA.
+template <bool Q5, int IL0, int NIL> struct StepK {
     __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
                                                const uint8_t *xs, int t, float (&acc)[4]) {
         constexpr int QS = Q5 ? 48 : 16;
@@ -175,8 +175,8 @@ template <bool Q5, int PART> struct StepK {
         zero4(p1[0]);
         zero4(p1[1]);
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int il = 2 * PART + i;
+        for (int i = 0; i < NIL; ++i) {
+            const int il = IL0 + i;
             const int j0 = 2 * il, j1 = 2 * il + 1;
             uint32_t sla = ka.sc(j0), slb = kb.sc(j0);
             uint32_t cla = hmul2_u(sla, H2_M1024), clb = hmul2_u(slb, H2_M1024);
@@ -213,22 +213,22 @@ template <bool Q5, int PART> struct StepK {
                 uint32_t b0, b1, b2, b3;
                 xfrag(xc, 64 * il + 16 * h, t, b0, b1);
                 xfrag(xc, 64 * il + 32 + 16 * h, t, b2, b3);
-                mma_16816(p1[h], alo, b0, b1, p1[h]);
-                mma_16816(p1[h], ahi, b2, b3, p1[h]);
+                mma_16816(p1[h], alo, b0, b1);
+                mma_16816(p1[h], ahi, b2, b3);
             }
         }
         float p2[4];
         zero4(p2);
-        if constexpr (PART == 0) {
+        if constexpr (IL0 == 0) {
             // thread t holds sub-blocks 2t, 2t+1: A = (m, m) for rows g, g+8; B = sums (hi | lo)
             const uint32_t sel = (t & 1) ? 0x4342u : 0x4140u;
             uint32_t am[4];
             am[0] = am[2] = hsub2_u(prmt(t < 2 ? ka.mA : ka.mB, 0x64646464u, sel), H2_1024);
             am[1] = am[3] = hsub2_u(prmt(t < 2 ? kb.mA : kb.mB, 0x64646464u, sel), H2_1024);
             const uint2 v = *reinterpret_cast<const uint2 *>(xs + 8 * t);
-            mma_16816(p2, am, v.x, v.y, p2);
+            mma_16816(p2, am, v.x, v.y);
         }
-        const float dma = PART == 0 ? hbits(ra + 2) : 0.f, dmb = PART == 0 ? hbits(rb + 2) : 0.f;
+        const float dma = IL0 == 0 ? hbits(ra + 2) : 0.f, dmb = IL0 == 0 ? hbits(rb + 2) : 0.f;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const float d = i < 2 ? da : db, dm = i < 2 ? dma : dmb;
@@ -240,15 +240,13 @@ template <bool Q5, int PART> struct StepK {
 template <> struct Step<VKF_DEQUANT_Q4_K> {
     __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
                                                const uint8_t *xs, int t, int part, int, float (&acc)[4]) {
-        if (part) StepK<false, 1>::run(ra, rb, xc, xs, t, acc);
-        else StepK<false, 0>::run(ra, rb, xc, xs, t, acc);
+        StepK<false, 0, 4>::run(ra, rb, xc, xs, t, acc);
     }
 };
 template <> struct Step<VKF_DEQUANT_Q5_K> {
     __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
                                                const uint8_t *xs, int t, int part, int, float (&acc)[4]) {
-        if (part) StepK<true, 1>::run(ra, rb, xc, xs, t, acc);
-        else StepK<true, 0>::run(ra, rb, xc, xs, t, acc);
+        StepK<true, 0, 4>::run(ra, rb, xc, xs, t, acc);
     }
 };
 
@@ -289,7 +287,7 @@ template <int IP> struct StepQ6 {
                     xfrag(xc, 128 * IP + 32 * s + 16 * h, t, b0, b1);
                     float p[4];
                     zero4(p);
-                    mma_16816(p, a, b0, b1, p);
+                    mma_16816(p, a, b0, b1);
                     const int is = 8 * IP + 2 * s + h;
                     const float fa = da * (float)sa[is], fb = db * (float)sb[is];
                     acc[0] = fmaf(fa, p[0], acc[0]);
@@ -305,8 +303,8 @@ template <int IP> struct StepQ6 {
 template <> struct Step<VKF_DEQUANT_Q6_K> {
     __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
                                                const uint8_t *, int t, int part, int, float (&acc)[4]) {
-        if (part) StepQ6<1>::run(ra, rb, xc, t, acc);
-        else StepQ6<0>::run(ra, rb, xc, t, acc);
+        StepQ6<0>::run(ra, rb, xc, t, acc);
+        StepQ6<1>::run(ra, rb, xc, t, acc);
     }
 };
 

@@ -11,7 +11,7 @@
 
 namespace vkf {
 int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void *Y, int y_f16, int64_t ldy, int M,
-                int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap);
+                int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap, int prefetch);
 size_t gemv_ws_floats(int sms);
 size_t gemv_counters(int N);
 int gemv_cols_per_launch(int K);
@@ -25,7 +25,7 @@ static bool gemv_format(int wtype) {
 // Decode path for M <= 8 (and, until the tensor-core GEMM covers a format,
 // for larger M in column groups).
 static int quant_linear_gemv(const void *W, int wtype, const void *X, int xtype, void *Y, int ytype, int M, int N,
-                             int K, int64_t ldx, int64_t ldy, cudaStream_t stream) {
+                             int K, int64_t ldx, int64_t ldy, cudaStream_t stream, unsigned flags) {
     DeviceState *ds = device_state();
     if (!ds) return VKF_ERR_NO_DEVICE;
     // Activations must reach the kernel as fp16 rows at 16-byte aligned
@@ -61,14 +61,15 @@ static int quant_linear_gemv(const void *W, int wtype, const void *X, int xtype,
         const void *xm = (const uint8_t *)xf + m0 * ldx_bytes;
         void *ym = (uint8_t *)Y + (size_t)m0 * ldy * (y_f16 ? 2 : 4);
         int rc = gemv_launch(wtype, W, xm, ldx_bytes, ym, y_f16, ldy, mc, N, K, stream,
-                             reinterpret_cast<float *>(scr + stage_bytes), ws_floats, cnt, ncnt);
+                             reinterpret_cast<float *>(scr + stage_bytes), ws_floats, cnt, ncnt,
+                             (flags & VKF_FLAG_STATIC_WEIGHTS) ? 1 : 0);
         if (rc) return rc;
     }
     return VKF_OK;
 }
 
 int quant_linear(const void *W, int wtype, const void *X, int xtype, void *Y, int ytype, int M, int N, int K,
-                 int64_t ldx, int64_t ldy, cudaStream_t stream) {
+                 int64_t ldx, int64_t ldy, cudaStream_t stream, unsigned flags) {
     if (!gemv_format(wtype)) return VKF_ERR_UNSUPPORTED;
     if (M < 0 || N < 0 || K < 0 || (xtype != VKF_X_F16 && xtype != VKF_X_Q8_1) ||
         (ytype != VKF_Y_F32 && ytype != VKF_Y_F16))
@@ -89,14 +90,20 @@ int quant_linear(const void *W, int wtype, const void *X, int xtype, void *Y, in
     if ((wtype == VKF_DEQUANT_Q4_K || wtype == VKF_DEQUANT_Q5_K) ? (wa & 3) : (wa & 1)) return VKF_ERR_BADPTR;
     if ((uintptr_t)Y & (ytype == VKF_Y_F16 ? 1 : 3)) return VKF_ERR_BADPTR;
     if (xtype == VKF_X_F16 && ((uintptr_t)X & 1)) return VKF_ERR_BADPTR;
-    return quant_linear_gemv(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, stream);
+    return quant_linear_gemv(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, stream, flags);
 }
 
 }  // namespace vkf
 
 extern "C" int vkflame_quant_linear(const void *W, int wtype, const void *X, int xtype, void *Y, int ytype, int M,
                                     int N, int K, int64_t ldx, int64_t ldy, void *stream) {
-    return vkf::set_status(vkf::quant_linear(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, (cudaStream_t)stream));
+    return vkf::set_status(vkf::quant_linear(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, (cudaStream_t)stream, 0));
+}
+
+extern "C" int vkflame_quant_linear_ex(const void *W, int wtype, const void *X, int xtype, void *Y, int ytype, int M,
+                                       int N, int K, int64_t ldx, int64_t ldy, unsigned flags, void *stream) {
+    return vkf::set_status(
+        vkf::quant_linear(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, (cudaStream_t)stream, flags));
 }
 
 // Tensor-core GEMM entry points (tcgen05); filled in by gemm_tc.cu.

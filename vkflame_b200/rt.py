@@ -45,6 +45,8 @@ _SIGS = {
     "vkflame_dispatch_dequant_async": ([C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_void_p], C.c_int),
     "vkflame_quant_linear": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
                               C.c_int, C.c_int, C.c_int, C.c_int64, C.c_int64, C.c_void_p], C.c_int),
+    "vkflame_quant_linear_ex": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                                 C.c_int, C.c_int, C.c_int, C.c_int64, C.c_int64, C.c_uint, C.c_void_p], C.c_int),
     "vkflame_quantize_q8_1": ([C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int64, C.c_void_p], C.c_int),
     "vkflame_linear_int8": ([C.c_void_p] * 7 + [C.c_int] * 4 + [C.c_void_p], C.c_int),
     "vkflame_get_last_error": ([], C.c_int),
@@ -59,7 +61,9 @@ def declared_symbols() -> list[str]:
 
 
 def load(path=None) -> C.CDLL:
-    p = path or LIBS["rt"]
+    import os
+    from pathlib import Path
+    p = Path(path or os.environ.get("VKFLAME_RT_LIB") or LIBS["rt"])
     if not p.exists():
         raise ImportError(f"[vkflame_b200] {p} not built (run __graft_entry__.build())")
     lib = C.CDLL(str(p), mode=C.RTLD_GLOBAL)
@@ -99,6 +103,15 @@ def dequant(src: int, dst: int, n_blocks: int, qtype: int, stream: int = 0) -> N
 def quant_linear(W: int, wtype: int, X: int, xtype: int, Y: int, ytype: int, M: int, N: int, K: int,
                  ldx: int, ldy: int, stream: int = 0) -> None:
     _check(lib().vkflame_quant_linear(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, stream), "quant_linear")
+
+
+FLAG_STATIC_WEIGHTS = 1
+
+
+def quant_linear_ex(W: int, wtype: int, X: int, xtype: int, Y: int, ytype: int, M: int, N: int, K: int,
+                    ldx: int, ldy: int, flags: int = 0, stream: int = 0) -> None:
+    _check(lib().vkflame_quant_linear_ex(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, flags, stream),
+           "quant_linear_ex")
 
 
 def quantize_q8_1(x: int, y: int, M: int, K: int, ldx: int, stream: int = 0) -> None:
