@@ -108,8 +108,8 @@ __device__ __forceinline__ void dq_super(const uint8_t *b, int v0, float (&o)[8]
     }
 }
 
-template <int QT, bool ALIGNED16>
-__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t *__restrict__ src, float *__restrict__ dst,
+template <int QT, bool ALIGNED16, bool F16OUT>
+__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t *__restrict__ src, void *__restrict__ dstv,
                                                       uint64_t nb) {
     constexpr bool SUPER = (QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K || QT == VKF_DEQUANT_Q6_K);
     constexpr int BB = (QT == VKF_DEQUANT_Q4_0) ? 18 : (QT == VKF_DEQUANT_Q4_1) ? 20 : (QT == VKF_DEQUANT_Q5_0) ? 22
@@ -131,7 +131,15 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t *__restrict_
         if (block >= nb) return;
         dq_block32<QT>(src + block * BB, v0, o);
     }
-    float *out = dst + unit * 256 + lane * 8;
+    if constexpr (F16OUT) {  // fp16 copy for the tensor-core GEMM (one rounding per value)
+        __half2 h[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(o[2 * i], o[2 * i + 1]);
+        *reinterpret_cast<uint4 *>(reinterpret_cast<__half *>(dstv) + unit * 256 + lane * 8) =
+            *reinterpret_cast<uint4 *>(h);
+        return;
+    }
+    float *out = reinterpret_cast<float *>(dstv) + unit * 256 + lane * 8;
     if constexpr (ALIGNED16) {
         reinterpret_cast<float4 *>(out)[0] = make_float4(o[0], o[1], o[2], o[3]);
         reinterpret_cast<float4 *>(out)[1] = make_float4(o[4], o[5], o[6], o[7]);
@@ -142,32 +150,35 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t *__restrict_
 }
 
 template <int QT>
-int launch_dequant(const void *src, void *dst, uint64_t nb, cudaStream_t stream) {
+int launch_dequant(const void *src, void *dst, uint64_t nb, cudaStream_t stream, bool f16out) {
     constexpr bool SUPER = (QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K || QT == VKF_DEQUANT_Q6_K);
     uint64_t units = SUPER ? nb : (nb + 7) / 8;
     uint64_t grid = (units + 7) / 8;
     if (grid == 0) return VKF_OK;
     if (grid > 0x7fffffffULL) return VKF_ERR_INVALID;
     bool aligned = ((uintptr_t)dst & 15) == 0;
-    if (aligned)
-        dequant_kernel<QT, true><<<(unsigned)grid, 256, 0, stream>>>((const uint8_t *)src, (float *)dst, nb);
+    if (f16out) {
+        if (!aligned) return VKF_ERR_BADPTR;
+        dequant_kernel<QT, true, true><<<(unsigned)grid, 256, 0, stream>>>((const uint8_t *)src, dst, nb);
+    } else if (aligned)
+        dequant_kernel<QT, true, false><<<(unsigned)grid, 256, 0, stream>>>((const uint8_t *)src, dst, nb);
     else
-        dequant_kernel<QT, false><<<(unsigned)grid, 256, 0, stream>>>((const uint8_t *)src, (float *)dst, nb);
+        dequant_kernel<QT, false, false><<<(unsigned)grid, 256, 0, stream>>>((const uint8_t *)src, dst, nb);
     return check_launch();
 }
 
 }  // namespace
 
-int dequant_launch(const void *src, void *dst, uint64_t nb, int qtype, cudaStream_t stream) {
+int dequant_launch(const void *src, void *dst, uint64_t nb, int qtype, cudaStream_t stream, bool f16out) {
     switch (qtype) {
-    case VKF_DEQUANT_Q4_0: return launch_dequant<VKF_DEQUANT_Q4_0>(src, dst, nb, stream);
-    case VKF_DEQUANT_Q4_1: return launch_dequant<VKF_DEQUANT_Q4_1>(src, dst, nb, stream);
-    case VKF_DEQUANT_Q8_0: return launch_dequant<VKF_DEQUANT_Q8_0>(src, dst, nb, stream);
-    case VKF_DEQUANT_Q5_0: return launch_dequant<VKF_DEQUANT_Q5_0>(src, dst, nb, stream);
-    case VKF_DEQUANT_Q4_K: return launch_dequant<VKF_DEQUANT_Q4_K>(src, dst, nb, stream);
-    case VKF_DEQUANT_Q5_K: return launch_dequant<VKF_DEQUANT_Q5_K>(src, dst, nb, stream);
-    case VKF_DEQUANT_Q6_K: return launch_dequant<VKF_DEQUANT_Q6_K>(src, dst, nb, stream);
-    case VKF_DEQUANT_Q8_1: return launch_dequant<VKF_DEQUANT_Q8_1>(src, dst, nb, stream);
+    case VKF_DEQUANT_Q4_0: return launch_dequant<VKF_DEQUANT_Q4_0>(src, dst, nb, stream, f16out);
+    case VKF_DEQUANT_Q4_1: return launch_dequant<VKF_DEQUANT_Q4_1>(src, dst, nb, stream, f16out);
+    case VKF_DEQUANT_Q8_0: return launch_dequant<VKF_DEQUANT_Q8_0>(src, dst, nb, stream, f16out);
+    case VKF_DEQUANT_Q5_0: return launch_dequant<VKF_DEQUANT_Q5_0>(src, dst, nb, stream, f16out);
+    case VKF_DEQUANT_Q4_K: return launch_dequant<VKF_DEQUANT_Q4_K>(src, dst, nb, stream, f16out);
+    case VKF_DEQUANT_Q5_K: return launch_dequant<VKF_DEQUANT_Q5_K>(src, dst, nb, stream, f16out);
+    case VKF_DEQUANT_Q6_K: return launch_dequant<VKF_DEQUANT_Q6_K>(src, dst, nb, stream, f16out);
+    case VKF_DEQUANT_Q8_1: return launch_dequant<VKF_DEQUANT_Q8_1>(src, dst, nb, stream, f16out);
     default: return VKF_ERR_INVALID;
     }
 }
@@ -183,7 +194,7 @@ extern "C" int vkflame_dispatch_dequant_async(const void *src, void *dst, uint64
     if (vkf::validate_device_range(src, in_bytes) != VKF_OK || vkf::validate_device_range(dst, out_bytes) != VKF_OK ||
         ((uintptr_t)dst & 3) || ((uintptr_t)src & 1))
         return vkf::set_status(VKF_ERR_BADPTR);
-    return vkf::set_status(vkf::dequant_launch(src, dst, n_blocks, quant_type, (cudaStream_t)stream));
+    return vkf::set_status(vkf::dequant_launch(src, dst, n_blocks, quant_type, (cudaStream_t)stream, false));
 }
 
 extern "C" int vkflame_dispatch_dequant(void *ctx, const void *src, void *dst, uint32_t n_blocks, int quant_type) {

@@ -9,6 +9,8 @@
 
 #include <cuda_fp16.h>
 
+#include <cstdlib>
+
 namespace vkf {
 int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void *Y, int y_f16, int64_t ldy, int M,
                 int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap, int prefetch);
@@ -16,6 +18,55 @@ size_t gemv_ws_floats(int sms);
 size_t gemv_counters(int N);
 int gemv_cols_per_launch(int K);
 int q8_1_to_f16(const void *src, void *dst, int M, int K, int64_t ldb, int64_t ldo, cudaStream_t stream);
+int dequant_launch(const void *src, void *dst, uint64_t nb, int qtype, cudaStream_t stream, bool f16out);
+int gemm_i8_tn(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, int M, int N, int K, const float *sx,
+               const float *sw, const void *bias, void *Y, int64_t ldy, int32_t *acc_out, int64_t ldacc, int act,
+               cudaStream_t stream);
+int gemm_f16_tn(const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K, float alpha, float beta,
+                const void *C, int64_t ldc, int c_f16, const void *bias, int act, void *Y, int64_t ldy, int y_f16,
+                cudaStream_t stream);
+int transpose(const void *src, int64_t lds, void *dst, int64_t ldd, int rows, int cols, int esize,
+              cudaStream_t stream);
+
+// M above which quantised linears take the tensor-core GEMM instead of the
+// decode GEMV (overridable with VKFLAME_GEMV_MAX_M for A/B comparisons).
+static int gemv_max_m() {
+    static const int v = [] {
+        const char *e = getenv("VKFLAME_GEMV_MAX_M");
+        return e ? atoi(e) : 8;
+    }();
+    return v;
+}
+
+static size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
+
+// Prefill path: widen W to fp16 (one rounding per weight) and X to fp16
+// rows, then the tcgen05 f16 GEMM with fp32 accumulation.
+static int quant_linear_gemm(const void *W, int wtype, const void *X, int xtype, void *Y, int ytype, int M, int N,
+                             int K, int64_t ldx, int64_t ldy, cudaStream_t stream) {
+    const size_t wbytes = align256((size_t)N * K * 2), xbytes = align256((size_t)M * K * 2);
+    uint8_t *scr = (uint8_t *)stream_scratch(stream, wbytes + xbytes);
+    if (!scr) return VKF_ERR_NOMEM;
+    int rc = dequant_launch(W, scr, (uint64_t)N * K / vkf_qtype_block_values(wtype), wtype, stream, true);
+    if (rc) return rc;
+    const void *xf = X;
+    int64_t lda = ldx;
+    if (xtype == VKF_X_Q8_1) {
+        rc = q8_1_to_f16(X, scr + wbytes, M, K, ldx, K, stream);
+        if (rc) return rc;
+        xf = scr + wbytes;
+        lda = K;
+    } else if (((uintptr_t)X & 15) || (ldx * 2) % 16) {
+        if (cudaMemcpy2DAsync(scr + wbytes, (size_t)K * 2, X, ldx * 2, (size_t)K * 2, M, cudaMemcpyDeviceToDevice,
+                              stream) != cudaSuccess)
+            return VKF_ERR_CUDA;
+        xf = scr + wbytes;
+        lda = K;
+    }
+    if (((size_t)K * 2) % 16) return VKF_ERR_UNSUPPORTED;
+    return gemm_f16_tn(xf, lda, scr, K, M, N, K, 1.0f, 0.0f, nullptr, 0, 0, nullptr, 0, Y, ldy,
+                       ytype == VKF_Y_F16, stream);
+}
 
 static bool gemv_format(int wtype) {
     return wtype == VKF_DEQUANT_Q4_0 || wtype == VKF_DEQUANT_Q8_0 || wtype == VKF_DEQUANT_Q4_K ||
@@ -90,6 +141,7 @@ int quant_linear(const void *W, int wtype, const void *X, int xtype, void *Y, in
     if ((wtype == VKF_DEQUANT_Q4_K || wtype == VKF_DEQUANT_Q5_K) ? (wa & 3) : (wa & 1)) return VKF_ERR_BADPTR;
     if ((uintptr_t)Y & (ytype == VKF_Y_F16 ? 1 : 3)) return VKF_ERR_BADPTR;
     if (xtype == VKF_X_F16 && ((uintptr_t)X & 1)) return VKF_ERR_BADPTR;
+    if (M > gemv_max_m()) return quant_linear_gemm(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, stream);
     return quant_linear_gemv(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, stream, flags);
 }
 
@@ -106,19 +158,108 @@ extern "C" int vkflame_quant_linear_ex(const void *W, int wtype, const void *X, 
         vkf::quant_linear(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, (cudaStream_t)stream, flags));
 }
 
-// Tensor-core GEMM entry points (tcgen05); filled in by gemm_tc.cu.
+
+// ---- linear_int8 and the generic linear dispatcher --------------------------
+
+namespace vkf {
+
+int linear_int8(const int8_t *X, const int8_t *W, const float *sx, const float *sw, const void *bias, void *Y,
+                int32_t *acc_out, int M, int N, int K, int act, cudaStream_t stream) {
+    if (M < 0 || N < 0 || K < 0 || act < 0 || act > 3) return VKF_ERR_INVALID;
+    if (M == 0 || N == 0) return VKF_OK;
+    if (!Y && !acc_out) return VKF_ERR_INVALID;
+    if (validate_device_range(X, (size_t)M * K) || validate_device_range(W, (size_t)N * K) ||
+        (sx && validate_device_range(sx, (size_t)M * 4)) || (sw && validate_device_range(sw, (size_t)N * 4)) ||
+        (bias && validate_device_range(bias, (size_t)N * 2)) || (Y && validate_device_range(Y, (size_t)M * N * 2)) ||
+        (acc_out && validate_device_range(acc_out, (size_t)M * N * 4)))
+        return VKF_ERR_BADPTR;
+    const int8_t *xa = X, *wa = W;
+    int64_t ld = K;
+    if (K % 16 || ((uintptr_t)X & 15) || ((uintptr_t)W & 15)) {
+        // TMA rows must start on 16-byte boundaries: pad K with zeros.
+        const int64_t kp = (K + 15) / 16 * 16;
+        uint8_t *scr = (uint8_t *)stream_scratch(stream, align256((size_t)M * kp) + align256((size_t)N * kp));
+        if (!scr) return VKF_ERR_NOMEM;
+        int8_t *xs = (int8_t *)scr, *ws = (int8_t *)(scr + align256((size_t)M * kp));
+        if (cudaMemsetAsync(scr, 0, align256((size_t)M * kp) + align256((size_t)N * kp), stream) != cudaSuccess ||
+            cudaMemcpy2DAsync(xs, kp, X, K, K, M, cudaMemcpyDeviceToDevice, stream) != cudaSuccess ||
+            cudaMemcpy2DAsync(ws, kp, W, K, K, N, cudaMemcpyDeviceToDevice, stream) != cudaSuccess)
+            return VKF_ERR_CUDA;
+        xa = xs;
+        wa = ws;
+        ld = kp;
+        K = (int)kp;
+    }
+    return gemm_i8_tn(xa, ld, wa, ld, M, N, K, sx, sw, bias, Y, N, acc_out, N, act, stream);
+}
+
+// runtime/dispatch.h:51-58 semantics, with the reference's ignored
+// arguments implemented (runtime/dispatch.cpp:262-267): op(A) is M x K, op(B)
+// is K x N, D = act(alpha * op(A) op(B) + beta * C), all row-major and packed.
+int dispatch_linear(const void *A, const void *B, const void *C, void *D, int M, int N, int K, int dtype, int transA,
+                    int transB, int act, const void *alpha, const void *beta, cudaStream_t stream) {
+    if (M < 0 || N < 0 || K < 0 || act < 0 || act > 3) return VKF_ERR_INVALID;
+    if (M == 0 || N == 0) return VKF_OK;
+    if (!A || !B || !D) return VKF_ERR_BADPTR;
+    const float al = alpha ? *(const float *)alpha : 1.0f, be = beta ? *(const float *)beta : 0.0f;
+    int esize;
+    switch (dtype) {
+    case VKF_DTYPE_FP16:
+    case VKF_DTYPE_FP16_FP32OUT: esize = 2; break;
+    case VKF_DTYPE_INT8: esize = 1; break;
+    default: return VKF_ERR_UNSUPPORTED;  // fp32 / bf16 inputs: not on this path
+    }
+    const int out_f16 = dtype == VKF_DTYPE_FP16 || dtype == VKF_DTYPE_INT8;
+    if (validate_device_range(A, (size_t)M * K * esize) || validate_device_range(B, (size_t)K * N * esize) ||
+        validate_device_range(D, (size_t)M * N * (out_f16 ? 2 : 4)) ||
+        (C && be != 0.0f && validate_device_range(C, (size_t)M * N * (out_f16 ? 2 : 4))))
+        return VKF_ERR_BADPTR;
+    // Bring both operands to K-major (A: M x K, B: N x K), padding K to 16 bytes.
+    const int64_t kp = ((int64_t)K * esize + 15) / 16 * 16 / esize;
+    const bool a_ok = !transA && kp == K && ((uintptr_t)A & 15) == 0;
+    const bool b_ok = transB && kp == K && ((uintptr_t)B & 15) == 0;
+    const size_t abytes = a_ok ? 0 : align256((size_t)M * kp * esize), bbytes = b_ok ? 0 : align256((size_t)N * kp * esize);
+    uint8_t *scr = nullptr;
+    if (abytes + bbytes) {
+        scr = (uint8_t *)stream_scratch(stream, abytes + bbytes);
+        if (!scr) return VKF_ERR_NOMEM;
+        if (kp != K && cudaMemsetAsync(scr, 0, abytes + bbytes, stream) != cudaSuccess) return VKF_ERR_CUDA;
+    }
+    const void *a = A, *b = B;
+    int rc = VKF_OK;
+    if (!a_ok) {
+        rc = transA ? transpose(A, M, scr, kp, K, M, esize, stream)  // stored K x M
+                    : (cudaMemcpy2DAsync(scr, kp * esize, A, (size_t)K * esize, (size_t)K * esize, M,
+                                         cudaMemcpyDeviceToDevice, stream) == cudaSuccess ? VKF_OK : VKF_ERR_CUDA);
+        a = scr;
+    }
+    if (rc) return rc;
+    if (!b_ok) {
+        rc = !transB ? transpose(B, N, scr + abytes, kp, K, N, esize, stream)  // stored K x N
+                     : (cudaMemcpy2DAsync(scr + abytes, kp * esize, B, (size_t)K * esize, (size_t)K * esize, N,
+                                          cudaMemcpyDeviceToDevice, stream) == cudaSuccess ? VKF_OK : VKF_ERR_CUDA);
+        b = scr + abytes;
+    }
+    if (rc) return rc;
+    if (dtype == VKF_DTYPE_INT8)
+        return gemm_i8_tn((const int8_t *)a, kp, (const int8_t *)b, kp, M, N, (int)kp, nullptr, nullptr, nullptr, D, N,
+                          nullptr, 0, act, stream);
+    return gemm_f16_tn(a, kp, b, kp, M, N, (int)kp, al, be, be != 0.0f ? C : nullptr, N, out_f16, nullptr, act, D, N,
+                       out_f16, stream);
+}
+
+}  // namespace vkf
+
 extern "C" int vkflame_linear_int8(const int8_t *X, const int8_t *W, const float *sx, const float *sw,
                                    const void *bias, void *Y, int32_t *acc_out, int M, int N, int K, int activation,
                                    void *stream) {
-    (void)X; (void)W; (void)sx; (void)sw; (void)bias; (void)Y; (void)acc_out; (void)M; (void)N; (void)K;
-    (void)activation; (void)stream;
-    return vkf::set_status(VKF_ERR_UNSUPPORTED);
+    return vkf::set_status(vkf::linear_int8(X, W, sx, sw, bias, Y, acc_out, M, N, K, activation, (cudaStream_t)stream));
 }
 
 extern "C" int vkflame_dispatch_linear(void *ctx, const void *A, const void *B, const void *C, void *D, int M, int N,
                                        int K, int dtype, int transA, int transB, int activation, const void *alpha,
                                        const void *beta, void *stream) {
-    (void)ctx; (void)A; (void)B; (void)C; (void)D; (void)M; (void)N; (void)K; (void)dtype; (void)transA;
-    (void)transB; (void)activation; (void)alpha; (void)beta; (void)stream;
-    return vkf::set_status(VKF_ERR_UNSUPPORTED);
+    (void)ctx;
+    return vkf::set_status(vkf::dispatch_linear(A, B, C, D, M, N, K, dtype, transA, transB, activation, alpha, beta,
+                                                (cudaStream_t)stream));
 }
