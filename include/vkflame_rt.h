@@ -116,6 +116,25 @@ int vkflame_quant_linear(const void *W, int wtype, const void *X, int xtype, voi
 int vkflame_quant_linear_ex(const void *W, int wtype, const void *X, int xtype, void *Y, int ytype,
                             int M, int N, int K, int64_t ldx, int64_t ldy, unsigned flags, void *stream);
 
+/* Allocation-free decode GEMV.  No counterpart in the reference: an addition
+ * for callers that must not allocate device memory (code inside an
+ * allocator callback, processes whose device memory is fully reserved up
+ * front, runtimes that forbid allocation after start-up).  Same result as
+ * vkflame_quant_linear with xtype VKF_X_F16, but its scratch is a fixed
+ * 576 KiB array in this library's device globals (held on every GPU that
+ * loads the library until the process exits) instead of per-stream arenas,
+ * and it never calls cudaMalloc/cudaFree.
+ *   Limits: 1 <= M <= 8, N <= 262144, M * (2K + 160 + K/8) <= 80 KiB,
+ *   X rows 16-byte aligned; anything else returns VKF_ERR_INVALID,
+ *   VKF_ERR_UNSUPPORTED or VKF_ERR_BADPTR and launches nothing.
+ * The first call on a device looks up the scratch's device address
+ * (cudaGetSymbolAddress); make that call before any stream capture.
+ * Every call shares the one scratch array: calls whose kernels may overlap
+ * on the GPU (different streams, or host threads) race and must be
+ * serialised by the caller. */
+int vkflame_quant_linear_noalloc(const void *W, int wtype, const void *X, void *Y, int ytype, int M, int N,
+                                 int K, int64_t ldx, int64_t ldy, void *stream);
+
 /* On-device fp32 -> Q8_1 quantiser (no reference counterpart: the reference
  * only decodes Q8_1, kernels/dequant_q8_1.glsl).  x is M x K fp32 (row stride
  * ldx elements), y receives M rows of K/32 blocks (36 B each), packed.

@@ -421,4 +421,33 @@ int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void
     }
 }
 
+// Same launch with the SM count and the kernel error word supplied by the
+// caller, so that nothing here allocates device memory (the allocation-free
+// entry point in noalloc.cu).
+int gemv_launch_raw(int wtype, const void *W, const void *X, int64_t ldx_bytes, void *Y, int y_f16, int64_t ldy,
+                    int M, int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap,
+                    int sms, unsigned *err) {
+    gemv::Args a{};
+    a.W = (const uint8_t *)W;
+    a.X = (const uint8_t *)X;
+    a.Y = Y;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.ldx_bytes = ldx_bytes;
+    a.ldy = ldy;
+    a.row_bytes = (int64_t)K / vkf_qtype_block_values(wtype) * vkf_qtype_block_bytes(wtype);
+    a.err = err;
+    a.y_f16 = y_f16;
+    a.prefetch = 0;
+    switch (wtype) {
+    case VKF_DEQUANT_Q4_0: return gemv::Launcher<VKF_DEQUANT_Q4_0>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    case VKF_DEQUANT_Q8_0: return gemv::Launcher<VKF_DEQUANT_Q8_0>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    case VKF_DEQUANT_Q4_K: return gemv::Launcher<VKF_DEQUANT_Q4_K>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    case VKF_DEQUANT_Q5_K: return gemv::Launcher<VKF_DEQUANT_Q5_K>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    case VKF_DEQUANT_Q6_K: return gemv::Launcher<VKF_DEQUANT_Q6_K>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    default: return VKF_ERR_UNSUPPORTED;
+    }
+}
+
 }  // namespace vkf

@@ -47,6 +47,8 @@ _SIGS = {
                               C.c_int, C.c_int, C.c_int, C.c_int64, C.c_int64, C.c_void_p], C.c_int),
     "vkflame_quant_linear_ex": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
                                  C.c_int, C.c_int, C.c_int, C.c_int64, C.c_int64, C.c_uint, C.c_void_p], C.c_int),
+    "vkflame_quant_linear_noalloc": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                      C.c_int, C.c_int64, C.c_int64, C.c_void_p], C.c_int),
     "vkflame_quantize_q8_1": ([C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int64, C.c_void_p], C.c_int),
     "vkflame_linear_int8": ([C.c_void_p] * 7 + [C.c_int] * 4 + [C.c_void_p], C.c_int),
     "vkflame_get_last_error": ([], C.c_int),
