@@ -5,7 +5,7 @@
 // kind::i8 (s8 x s8 -> s32) serves linear_int8 (kernels/linear_int8.glsl,
 // whose int32 accumulator this reproduces bit for bit); kind::f16 (f16 x f16
 // -> f32) serves fp16 GEMMs and quantised-weight prefill (weights widened to
-// fp16 first).  The reference computes these with one thread per output and
+// fp16 first); kind::tf32 serves fp32 GEMMs.  The reference computes these with one thread per output and
 // a K-serial loop (linear_int8.glsl:48-101, linear_fp16.glsl:38-51).
 //
 // One 128 x BN output tile per CTA, 192 threads:
@@ -69,13 +69,14 @@ __device__ __forceinline__ float activation(int act, float x) {
     }
 }
 
-template <bool I8, int BN, int NS>
+template <int KIND, int BN, int NS>
 __global__ void __launch_bounds__(NT, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
                 const __grid_constant__ Epi e) {
+    constexpr bool I8 = KIND == tc::KIND_I8;
     constexpr int A_BYTES = BM * BKB, B_BYTES = BN * BKB, STAGE = A_BYTES + B_BYTES;
-    constexpr int KE = I8 ? 128 : 64;  // elements of K per stage
-    constexpr uint32_t IDESC = tc::instr_desc(I8, BM, BN);
+    constexpr int KE = I8 ? 128 : KIND == tc::KIND_TF32 ? 32 : 64;  // elements of K per stage
+    constexpr uint32_t IDESC = tc::instr_desc(KIND, BM, BN);
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + NS * STAGE);
@@ -118,7 +119,7 @@ __global__ void __launch_bounds__(NT, 1)
             const uint32_t sa = smem_addr(smem + s * STAGE), sb = sa + A_BYTES;
 #pragma unroll
             for (int kk = 0; kk < BKB / 32; ++kk)
-                tc::mma<I8>(tmem, tc::smem_desc_sw128(sa + kk * 32), tc::smem_desc_sw128(sb + kk * 32), IDESC,
+                tc::mma<KIND>(tmem, tc::smem_desc_sw128(sa + kk * 32), tc::smem_desc_sw128(sb + kk * 32), IDESC,
                             (kb | kk) != 0);
             tc::commit(&empty[s]);
         }
@@ -192,22 +193,25 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // elements; box = (box_cols x box_rows), 128-byte swizzle.
 static bool make_map(CUtensorMap *m, const void *base, int esize, int64_t rows, int64_t cols, int64_t ld,
                      int box_cols, int box_rows) {
+    const CUtensorMapDataType dt = esize == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)(ld * esize)};
     cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(m, esize == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+    CUresult r = fn(m, dt, 2,
                     const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
-template <bool I8, int BN, int NS>
+template <int KIND, int BN, int NS>
 static int launch(const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K, const Epi &e,
                   cudaStream_t stream) {
-    const int esize = I8 ? 1 : 2, KE = I8 ? 128 : 64;
+    const int esize = KIND == tc::KIND_I8 ? 1 : KIND == tc::KIND_TF32 ? 4 : 2, KE = BKB / esize;
     CUtensorMap ta, tb;
     if (!make_map(&ta, A, esize, M, K, lda, KE, BM) || !make_map(&tb, B, esize, N, K, ldb, KE, BN))
         return VKF_ERR_INVALID;
@@ -216,11 +220,11 @@ static int launch(const void *A, int64_t lda, const void *B, int64_t ldb, int M,
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr[dev]) {
-        cudaFuncSetAttribute(gemm_kernel<I8, BN, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(gemm_kernel<KIND, BN, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr[dev] = true;
     }
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-    gemm_kernel<I8, BN, NS><<<grid, NT, smem, stream>>>(ta, tb, M, N, K, e);
+    gemm_kernel<KIND, BN, NS><<<grid, NT, smem, stream>>>(ta, tb, M, N, K, e);
     return check_launch();
 }
 
@@ -234,14 +238,14 @@ static bool tma_ok(const void *p, int64_t ld, int esize) {
 // D = epilogue(A x B^T); A: M x K (lda), B: N x K (ldb), both int8.
 int gemm_i8_tn(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, int M, int N, int K, const float *sx,
                const float *sw, const void *bias, void *Y, int64_t ldy, int32_t *acc_out, int64_t ldacc, int act,
-               cudaStream_t stream) {
+               cudaStream_t stream, int y_f16) {
     DeviceState *ds = device_state();
     if (!ds) return VKF_ERR_NO_DEVICE;
     if (!tma_ok(A, lda, 1) || !tma_ok(B, ldb, 1)) return VKF_ERR_BADPTR;
     gemm::Epi e{};
     e.Y = Y;
     e.ldy = ldy;
-    e.y_f16 = 1;
+    e.y_f16 = y_f16;
     e.acc_out = acc_out;
     e.ldacc = ldacc;
     e.sx = sx;
@@ -249,7 +253,7 @@ int gemm_i8_tn(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, int M
     e.bias = (const __half *)bias;
     e.act = act;
     e.err = ds->d_error;
-    return gemm::launch<true, 256, 4>(A, lda, B, ldb, M, N, K, e, stream);
+    return gemm::launch<tc::KIND_I8, 256, 4>(A, lda, B, ldb, M, N, K, e, stream);
 }
 
 // D = act(alpha * A x B^T + beta * C + bias); A: M x K f16, B: N x K f16.
@@ -271,7 +275,29 @@ int gemm_f16_tn(const void *A, int64_t lda, const void *B, int64_t ldb, int M, i
     e.bias = (const __half *)bias;
     e.act = act;
     e.err = ds->d_error;
-    return gemm::launch<false, 256, 4>(A, lda, B, ldb, M, N, K, e, stream);
+    return gemm::launch<tc::KIND_F16, 256, 4>(A, lda, B, ldb, M, N, K, e, stream);
+}
+
+// As gemm_f16_tn with fp32 operands (tensor-core tf32: 10-bit mantissa products, fp32 accumulation).
+int gemm_tf32_tn(const float *A, int64_t lda, const float *B, int64_t ldb, int M, int N, int K, float alpha,
+                 float beta, const void *C, int64_t ldc, int c_f16, const void *bias, int act, void *Y, int64_t ldy,
+                 int y_f16, cudaStream_t stream) {
+    DeviceState *ds = device_state();
+    if (!ds) return VKF_ERR_NO_DEVICE;
+    if (!tma_ok(A, lda, 4) || !tma_ok(B, ldb, 4)) return VKF_ERR_BADPTR;
+    gemm::Epi e{};
+    e.Y = Y;
+    e.ldy = ldy;
+    e.y_f16 = y_f16;
+    e.alpha = alpha;
+    e.beta = beta;
+    e.C = C;
+    e.ldc = ldc;
+    e.c_f16 = c_f16;
+    e.bias = (const __half *)bias;
+    e.act = act;
+    e.err = ds->d_error;
+    return gemm::launch<tc::KIND_TF32, 256, 4>(A, lda, B, ldb, M, N, K, e, stream);
 }
 
 }  // namespace vkf

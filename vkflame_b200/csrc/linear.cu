@@ -21,7 +21,10 @@ int q8_1_to_f16(const void *src, void *dst, int M, int K, int64_t ldb, int64_t l
 int dequant_launch(const void *src, void *dst, uint64_t nb, int qtype, cudaStream_t stream, bool f16out);
 int gemm_i8_tn(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, int M, int N, int K, const float *sx,
                const float *sw, const void *bias, void *Y, int64_t ldy, int32_t *acc_out, int64_t ldacc, int act,
-               cudaStream_t stream);
+               cudaStream_t stream, int y_f16 = 1);
+int gemm_tf32_tn(const float *A, int64_t lda, const float *B, int64_t ldb, int M, int N, int K, float alpha,
+                 float beta, const void *C, int64_t ldc, int c_f16, const void *bias, int act, void *Y, int64_t ldy,
+                 int y_f16, cudaStream_t stream);
 int gemm_f16_tn(const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K, float alpha, float beta,
                 const void *C, int64_t ldc, int c_f16, const void *bias, int act, void *Y, int64_t ldy, int y_f16,
                 cudaStream_t stream);
@@ -207,7 +210,8 @@ int dispatch_linear(const void *A, const void *B, const void *C, void *D, int M,
     case VKF_DTYPE_FP16:
     case VKF_DTYPE_FP16_FP32OUT: esize = 2; break;
     case VKF_DTYPE_INT8: esize = 1; break;
-    default: return VKF_ERR_UNSUPPORTED;  // fp32 / bf16 inputs: not on this path
+    case VKF_DTYPE_FP32: esize = 4; break;
+    default: return VKF_ERR_UNSUPPORTED;  // bf16 inputs: not on this path
     }
     const int out_f16 = dtype == VKF_DTYPE_FP16 || dtype == VKF_DTYPE_INT8;
     if (validate_device_range(A, (size_t)M * K * esize) || validate_device_range(B, (size_t)K * N * esize) ||
@@ -241,6 +245,9 @@ int dispatch_linear(const void *A, const void *B, const void *C, void *D, int M,
         b = scr + abytes;
     }
     if (rc) return rc;
+    if (dtype == VKF_DTYPE_FP32)
+        return gemm_tf32_tn((const float *)a, kp, (const float *)b, kp, M, N, (int)kp, al, be, be != 0.0f ? C : nullptr,
+                            N, 0, nullptr, act, D, N, 0, stream);
     if (dtype == VKF_DTYPE_INT8)
         return gemm_i8_tn((const int8_t *)a, kp, (const int8_t *)b, kp, M, N, (int)kp, nullptr, nullptr, nullptr, D, N,
                           nullptr, 0, act, stream);

@@ -29,19 +29,30 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
     return d;
 }
 
-// kind::f16 with f16 inputs and f32 accumulator, or kind::i8 with s8 inputs
-// and s32 accumulator; both operands K-major.
-__host__ __device__ constexpr uint32_t instr_desc(bool i8, int M, int N) {
-    return (uint32_t)((i8 ? 2u : 1u) << 4) | (uint32_t)((i8 ? 1u : 0u) << 7) | (uint32_t)((i8 ? 1u : 0u) << 10) |
-           (uint32_t)((N >> 3) << 17) | (uint32_t)((M >> 4) << 24);
+// Operand kinds: f16 x f16 -> f32 (kind::f16), s8 x s8 -> s32 (kind::i8),
+// tf32 x tf32 -> f32 (kind::tf32, fp32 operands in memory).
+enum Kind { KIND_F16 = 0, KIND_I8 = 1, KIND_TF32 = 2 };
+
+// Both operands K-major.  A/B format: f16 = 0, tf32 = 2 (kind::f16 family);
+// s8 = 1 (kind::i8).  D format: f32 = 1, s32 = 2.
+__host__ __device__ constexpr uint32_t instr_desc(int kind, int M, int N) {
+    return (uint32_t)((kind == KIND_I8 ? 2u : 1u) << 4) |
+           (uint32_t)((kind == KIND_I8 ? 1u : kind == KIND_TF32 ? 2u : 0u) << 7) |
+           (uint32_t)((kind == KIND_I8 ? 1u : kind == KIND_TF32 ? 2u : 0u) << 10) | (uint32_t)((N >> 3) << 17) |
+           (uint32_t)((M >> 4) << 24);
 }
 
-template <bool I8>
+template <int KIND>
 __device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-    if constexpr (I8)
+    if constexpr (KIND == KIND_I8)
         asm volatile(
             "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
             " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+    else if constexpr (KIND == KIND_TF32)
+        asm volatile(
+            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+            " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
             "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
     else
         asm volatile(
