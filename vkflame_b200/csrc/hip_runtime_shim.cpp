@@ -432,7 +432,7 @@ hipError_t hipPeekAtLastError(void) { return t_last; }
 //   mul_mat + <quant>: (vx, vy Q8_1, dst f32, ncols_x = K, nrows_x = N,
 //       ncols_y, nrows_y = M)  -> vkflame_quant_linear (fused dequant GEMV/GEMM)
 //   mul_mat + f16:     (A, B, dst, K, N, -, M)  -> vkflame_dispatch_linear (TN)
-//   dequantize:        q4_0/q4_1/q5_0: (vx, y, int nb32); q8_0: (vx, y, int nb)
+//   dequantize_*:      q4_0/q4_1/q5_0: (vx, y, int nb32); q8_0: (vx, y, int nb)
 //       or (vx, y, int64 k) when blockDim.x != 32; K-quants: (vx, y), nb = gridDim.x
 // Other names (activations, norms, rope, ...: not on this path) are logged
 // and skipped with hipSuccess, as the reference did (:849-851); with
@@ -489,7 +489,7 @@ hipError_t hipLaunchKernel(const void *func, vkf_dim3 gridDim, vkf_dim3 blockDim
         logf("mul_mat kernel %s: weight format not on this path\n", name.c_str());
         return ret(strict() ? hipErrorInvalidValue : hipSuccess);
     }
-    if (qt >= 0 && !has("quantize")) {
+    if (qt >= 0 && has("dequantize")) {
         uint64_t nb;
         switch (qt) {
         case VKF_DEQUANT_Q4_0:
