@@ -2,7 +2,7 @@
 """Benchmark of the quantised-linear hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload stack|gemv] [--no-extras] [--no-cpu-baseline]
+                    [--workload stack|<config 1-4 case>] [--no-extras] [--no-cpu-baseline]
 
 Default workload: the 48-layer linear stack of a
 Qwen2-architecture 14B decoder with Q4_K_M-style random weights (Q6_K for
@@ -11,8 +11,13 @@ column-sharded over the ranks with an NCCL all-gather of every linear
 group's output slices.  A step is one token: every weight of the stack is
 streamed once.  Metric: aggregate weight-streaming GB/s.
 
-Prints ONE JSON line (rank 0).  See DESIGN.md ("Measurement") for the
-definition of every field.  Inputs are seeded synthetic ggml blocks with the
+Prints ONE JSON line (rank 0): the base fields, plus "roofline" (per-GPU
+weight bytes per token / device time per token against the measured HBM
+copy bandwidth), "cpu_baseline" (the CPU restatement of the reference
+pipeline on this host's cores, bounded sample), "e2e" (the same metric with a
+pinned-host input copy and a logits read-back inside the timed region),
+"gpu_launches" and "clocks".  `--workload <case>` runs one config 1-4 case
+alone and prints its device time (used for ncu captures).  Inputs are seeded synthetic ggml blocks with the
 benchmark configs' distributions (vkflame_b200/synth.py): no model weights
 or datasets exist on this machine.
 """
@@ -331,34 +336,44 @@ def graph_time(fn, iters=20):
     return e0.elapsed_time(e1) / iters
 
 
-def sub_benchmarks():
-    """Configs 1-4 at one shape each (device time, CUDA graphs, weights rotated past L2)."""
+GEMV_CASES = {"config3_q4K_gate_up_M1": (S.Q4_K, 5120, 13824, 1),
+              "config3_q4K_gate_up_M8": (S.Q4_K, 5120, 13824, 8),
+              "config3_q4K_qo_M1": (S.Q4_K, 5120, 5120, 1),
+              "config3_q4K_down_M1": (S.Q4_K, 13824, 5120, 1),
+              "config1_q4_0_M1": (S.Q4_0, 4096, 4096, 1),
+              "config1_q4_0_M32": (S.Q4_0, 4096, 4096, 32),
+              "q8_0_gate_up_M1": (S.Q8_0, 5120, 13824, 1),
+              "q6K_down_M1": (S.Q6_K, 13824, 5120, 1)}
+
+
+def bench_gemv_case(name, iters_per_copy=4):
+    """One quantised linear (config 1/3 shapes): device time per call under a
+    CUDA graph, with the weights rotated over copies that together exceed 3x L2
+    so every call streams its weights from HBM."""
     import torch
     from vkflame_b200 import rt
-    out = {}
+    q, K, N, M = GEMV_CASES[name]
     l2 = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
-    for name, q, K, N, M in [("config3_q4K_gate_up_M1", S.Q4_K, 5120, 13824, 1),
-                             ("config3_q4K_gate_up_M8", S.Q4_K, 5120, 13824, 8),
-                             ("config3_q4K_qo_M1", S.Q4_K, 5120, 5120, 1),
-                             ("config3_q4K_down_M1", S.Q4_K, 13824, 5120, 1),
-                             ("config1_q4_0_M1", S.Q4_0, 4096, 4096, 1),
-                             ("config1_q4_0_M32", S.Q4_0, 4096, 4096, 32),
-                             ("q8_0_gate_up_M1", S.Q8_0, 5120, 13824, 1)]:
-        wb = N * S.row_bytes(q, K)
-        copies = max(2, int(np.ceil(3 * l2 / wb)))
-        ws = [make_quant_weight_gpu(q, N, K, seed=i) for i in range(copies)]
-        x = torch.randn((M, K), device="cuda").half()
-        y = torch.empty((M, N), device="cuda", dtype=torch.float16)
-        it = [0]
-        def fn(sp):
-            w = ws[it[0] % copies]
-            it[0] += 1
-            rt.quant_linear_ex(w.data_ptr(), q, x.data_ptr(), rt.X_F16, y.data_ptr(), rt.Y_F16, M, N, K, K, N,
-                               rt.FLAG_STATIC_WEIGHTS, sp)
-        ms = graph_time(fn, iters=4 * copies)
-        out[name] = {"us": ms * 1e3, "GB/s": (wb + M * K * 2 + M * N * 2) / (ms * 1e-3) / 1e9}
-        del ws
-    # config 2: int8 linear with per-row / per-channel scales and bias (hipblasLt BIAS epilogue)
+    wb = N * S.row_bytes(q, K)
+    copies = max(2, int(np.ceil(3 * l2 / wb)))
+    ws = [make_quant_weight_gpu(q, N, K, seed=i) for i in range(copies)]
+    x = torch.randn((M, K), device="cuda").half()
+    y = torch.empty((M, N), device="cuda", dtype=torch.float16)
+    it = [0]
+    def fn(sp):
+        w = ws[it[0] % copies]
+        it[0] += 1
+        rt.quant_linear_ex(w.data_ptr(), q, x.data_ptr(), rt.X_F16, y.data_ptr(), rt.Y_F16, M, N, K, K, N,
+                           rt.FLAG_STATIC_WEIGHTS, sp)
+    ms = graph_time(fn, iters=iters_per_copy * copies)
+    return {"us": ms * 1e3, "GB/s": (wb + M * K * 2 + M * N * 2) / (ms * 1e-3) / 1e9}
+
+
+def bench_int8_linear():
+    """Config 2: int8 linear with per-row / per-channel scales and bias (the
+    hipblasLt BIAS-epilogue call)."""
+    import torch
+    from vkflame_b200 import rt
     M, N, K = 512, 11008, 4096
     xi = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
     wi = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda")
@@ -367,8 +382,13 @@ def sub_benchmarks():
     yi = torch.empty((M, N), device="cuda", dtype=torch.float16)
     ms = graph_time(lambda sp: rt.linear_int8(xi.data_ptr(), wi.data_ptr(), sx.data_ptr(), sw.data_ptr(),
                                               bias.data_ptr(), yi.data_ptr(), 0, M, N, K, 0, sp))
-    out["config2_int8_linear_M512"] = {"us": ms * 1e3, "TOPS": 2 * M * N * K / (ms * 1e-3) / 1e12}
-    # config 4: fp32 X -> on-device Q8_1 -> Q8_0 x Q8_1 prefill GEMM, fp32 out
+    return {"us": ms * 1e3, "TOPS": 2 * M * N * K / (ms * 1e-3) / 1e12}
+
+
+def bench_q8_prefill():
+    """Config 4: fp32 X -> on-device Q8_1 -> Q8_0 x Q8_1 prefill GEMM, fp32 out."""
+    import torch
+    from vkflame_b200 import rt
     M, N, K = 512, 13824, 5120
     wq = make_quant_weight_gpu(S.Q8_0, N, K, 7)
     xf = torch.randn((M, K), device="cuda")
@@ -379,7 +399,17 @@ def sub_benchmarks():
         rt.quant_linear(wq.data_ptr(), S.Q8_0, xq.data_ptr(), rt.X_Q8_1, yo.data_ptr(), rt.Y_F32, M, N, K, K // 32,
                         N, sp)
     ms = graph_time(c4, iters=5)
-    out["config4_q8_0_x_q8_1_M512"] = {"us": ms * 1e3, "TOPS": 2 * M * N * K / (ms * 1e-3) / 1e12}
+    return {"us": ms * 1e3, "TOPS": 2 * M * N * K / (ms * 1e-3) / 1e12}
+
+
+SUB_CASES = dict({n: (lambda n=n: bench_gemv_case(n)) for n in GEMV_CASES},
+                 config2_int8_linear_M512=bench_int8_linear, config4_q8_0_x_q8_1_M512=bench_q8_prefill)
+
+
+def sub_benchmarks(names=None):
+    """Configs 1-4 at one shape each (device time, CUDA graphs)."""
+    from vkflame_b200 import rt
+    out = {n: SUB_CASES[n]() for n in (names or SUB_CASES)}
     rt.check_kernel_errors()
     return out
 
@@ -416,7 +446,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="stack", choices=["stack"])
+    ap.add_argument("--workload", default="stack", choices=["stack"] + list(SUB_CASES),
+                    help="stack (config 5, the headline) or one config 1-4 case alone (device time only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 1-4 sub-benchmarks")
     args = ap.parse_args()
@@ -437,6 +468,11 @@ def main():
                 "cpu_baseline": cb,
                 "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
+        return
+
+    if args.workload != "stack":
+        init_dist(world, local)
+        print(json.dumps({"workload": args.workload, **sub_benchmarks([args.workload])[args.workload]}))
         return
 
     dist = init_dist(world, local)

@@ -47,6 +47,7 @@ struct Epi {
     const void *C;
     int64_t ldc;
     int c_f16;
+    int vec;            // VEC_* bits
     unsigned *err;
 };
 
@@ -66,6 +67,55 @@ __device__ __forceinline__ float activation(int act, float x) {
     case VKF_ACT_RELU: return x > 0.0f ? x : 0.0f;
     case VKF_ACT_GELU_ERF: return 0.5f * x * (1.0f + erf_as(x * 0.70710678118654f));
     default: return x;
+    }
+}
+
+// Epi::vec bits: the operand's rows are 16-byte aligned (base and stride).
+enum { VEC_Y = 1, VEC_ACC = 2, VEC_C = 4, VEC_SW = 8, VEC_BIAS = 16 };
+
+__device__ __forceinline__ uint32_t h2_bits(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// 32 values from p[col0 ..] (ncol valid, 1.0 / 0.0 past the end or when p is null).
+__device__ __forceinline__ void load_f32_chunk(const float *p, int col0, int ncol, bool vec, float (&o)[32]) {
+    if (!p) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[j] = 1.0f;
+        return;
+    }
+    if (vec) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            const float4 t = __ldg(reinterpret_cast<const float4 *>(p + col0 + j));
+            o[j] = t.x;
+            o[j + 1] = t.y;
+            o[j + 2] = t.z;
+            o[j + 3] = t.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[j] = j < ncol ? p[col0 + j] : 1.0f;
+    }
+}
+
+__device__ __forceinline__ void load_f16_chunk(const __half *p, int col0, int ncol, bool vec, float (&o)[32]) {
+    if (vec) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+            const uint4 t = __ldg(reinterpret_cast<const uint4 *>(p + col0 + j));
+            const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+                o[j + 2 * i] = f.x;
+                o[j + 2 * i + 1] = f.y;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[j] = j < ncol ? __half2float(p[col0 + j]) : 0.0f;
     }
 }
 
@@ -136,32 +186,83 @@ __global__ void __launch_bounds__(NT, 1)
         for (int c = 0; c < BN / 32; ++c) {
             uint32_t r[32];
             tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 32 * c, r);
-            if (!ok || row >= M) continue;
             const int col0 = n0 + 32 * c;
+            if (!ok || row >= M || col0 >= N) continue;
+            // This thread owns 32 consecutive columns of one output row: with
+            // 16-byte aligned rows every read and write below is a vector
+            // access along the row; ragged or unaligned chunks go scalar.
+            const bool full = col0 + 32 <= N;
+            const int ncol = full ? 32 : N - col0;
+            float v[32];
+            if constexpr (I8) {
+                if (e.acc_out) {
+                    int32_t *ap = e.acc_out + (int64_t)row * e.ldacc + col0;
+                    if (full && (e.vec & VEC_ACC)) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int col = col0 + j;
-                if (col >= N) break;
-                float v;
-                if constexpr (I8) {
-                    const int32_t acc = (int32_t)r[j];
-                    if (e.acc_out) e.acc_out[(int64_t)row * e.ldacc + col] = acc;
-                    v = (float)acc;
-                    v = __fmul_rn(v, sxr);
-                    if (e.sw) v = __fmul_rn(v, e.sw[col]);
-                } else {
-                    v = __fmul_rn(e.alpha, __uint_as_float(r[j]));
-                    if (e.C && e.beta != 0.0f) {
-                        const float cv = e.c_f16 ? __half2float(reinterpret_cast<const __half *>(e.C)[(int64_t)row * e.ldc + col])
-                                                 : reinterpret_cast<const float *>(e.C)[(int64_t)row * e.ldc + col];
-                        v = __fadd_rn(v, __fmul_rn(e.beta, cv));
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<uint4 *>(ap + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < ncol) ap[j] = (int32_t)r[j];
                     }
                 }
-                if (e.bias) v = __fadd_rn(v, __half2float(e.bias[col]));
-                v = activation(e.act, v);
-                if (e.Y) {
-                    if (e.y_f16) reinterpret_cast<__half *>(e.Y)[(int64_t)row * e.ldy + col] = __float2half_rn(v);
-                    else reinterpret_cast<float *>(e.Y)[(int64_t)row * e.ldy + col] = v;
+                float swv[32];
+                load_f32_chunk(e.sw, col0, ncol, full && (e.vec & VEC_SW), swv);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(__fmul_rn((float)(int32_t)r[j], sxr), swv[j]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(e.alpha, __uint_as_float(r[j]));
+                if (e.C && e.beta != 0.0f) {
+                    float cv[32];
+                    if (e.c_f16)
+                        load_f16_chunk(reinterpret_cast<const __half *>(e.C) + (int64_t)row * e.ldc, col0, ncol,
+                                       full && (e.vec & VEC_C), cv);
+                    else
+                        load_f32_chunk(reinterpret_cast<const float *>(e.C) + (int64_t)row * e.ldc, col0, ncol,
+                                       full && (e.vec & VEC_C), cv);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], __fmul_rn(e.beta, cv[j]));
+                }
+            }
+            if (e.bias) {
+                float bv[32];
+                load_f16_chunk(e.bias, col0, ncol, full && (e.vec & VEC_BIAS), bv);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], bv[j]);
+            }
+            if (e.act) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = activation(e.act, v[j]);
+            }
+            if (!e.Y) continue;
+            if (e.y_f16) {
+                __half *yp = reinterpret_cast<__half *>(e.Y) + (int64_t)row * e.ldy + col0;
+                if (full && (e.vec & VEC_Y)) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 8) {
+                        uint4 o;
+                        o.x = h2_bits(v[j], v[j + 1]);
+                        o.y = h2_bits(v[j + 2], v[j + 3]);
+                        o.z = h2_bits(v[j + 4], v[j + 5]);
+                        o.w = h2_bits(v[j + 6], v[j + 7]);
+                        *reinterpret_cast<uint4 *>(yp + j) = o;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < ncol) yp[j] = __float2half_rn(v[j]);
+                }
+            } else {
+                float *yp = reinterpret_cast<float *>(e.Y) + (int64_t)row * e.ldy + col0;
+                if (full && (e.vec & VEC_Y)) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4 *>(yp + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < ncol) yp[j] = v[j];
                 }
             }
         }
@@ -208,9 +309,17 @@ static bool make_map(CUtensorMap *m, const void *base, int esize, int64_t rows, 
     return r == CUDA_SUCCESS;
 }
 
+static bool rows16(const void *p, int64_t ld, int esize) {
+    return ((uintptr_t)p & 15) == 0 && (ld * esize) % 16 == 0;
+}
+
 template <int KIND, int BN, int NS>
-static int launch(const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K, const Epi &e,
+static int launch(const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K, Epi e,
                   cudaStream_t stream) {
+    e.vec = (e.Y && rows16(e.Y, e.ldy, e.y_f16 ? 2 : 4) ? VEC_Y : 0) |
+            (e.acc_out && rows16(e.acc_out, e.ldacc, 4) ? VEC_ACC : 0) |
+            (e.C && rows16(e.C, e.ldc, e.c_f16 ? 2 : 4) ? VEC_C : 0) | (e.sw && rows16(e.sw, 0, 4) ? VEC_SW : 0) |
+            (e.bias && rows16(e.bias, 0, 2) ? VEC_BIAS : 0);
     const int esize = KIND == tc::KIND_I8 ? 1 : KIND == tc::KIND_TF32 ? 4 : 2, KE = BKB / esize;
     CUtensorMap ta, tb;
     if (!make_map(&ta, A, esize, M, K, lda, KE, BM) || !make_map(&tb, B, esize, N, K, ldb, KE, BN))

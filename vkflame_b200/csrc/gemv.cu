@@ -7,32 +7,29 @@
 // GEMM (shim/hip_runtime_shim.cpp:1102-1172, kernels/linear_fp16_fp32out.glsl).
 // Here the packed blocks are read once from HBM and decoded in registers.
 //
-// Measured on B200 (copy microbenchmarks): streaming reads reach ~7.1 TB/s
-// when each request run is kilobytes long, but a 128-row x 144..272-byte
-// K-step (the natural MMA tile of a ggml row-major matrix) held DRAM to
-// 2.6-4.4 TB/s.  The kernel therefore works on items of 16 rows x a K-range
-// of up to ~3 KB of each row (the whole row for K = 5120 Q4_K):
+// Work items are 16 rows x a K-range of each row (a run of ~0.5-1.6 KB per
+// row: short K-steps of many rows hold DRAM well below its streaming rate on
+// B200).  One CTA per SM:
 //
 //   warp CW       producer: one TMA bulk copy per row per item into an
-//                 NST-deep ring, completion by mbarrier transaction bytes.
-//   warps 0..CW-1 consumers: take the work units (one super-block, or eight
-//                 32-value blocks, of the 16 rows) round-robin, decode them
-//                 into m16n8k16 fragments (gemv_q.cuh: A = the 16 weight
-//                 rows, N = the M <= 8 activation columns) and keep a per-warp
-//                 fp32 accumulator; they never wait for each other, and the
-//                 last warp to finish a row block reduces the CW partials.
+//                 NST-deep ring, completion by mbarrier transaction bytes;
+//                 with static weights it starts before the previous kernel
+//                 on the stream has finished (programmatic dependent launch).
+//   warps 0..CW-1 consumers: take the 256-value units of the item sequence
+//                 round-robin, decode them into m16n8k16 fragments
+//                 (gemv_q.cuh) and keep a per-warp fp32 accumulator for the
+//                 current row block.  At the end of a row block a warp parks
+//                 its partial in the block's shared-memory slot and goes on;
+//                 the last warp to arrive (one shared atomic per warp) sums
+//                 the slot in warp order (deterministic) and stores Y.  No
+//                 consumer ever waits for another.
 //
-// The activations X (M x K fp16) stay resident in shared memory for the whole
-// CTA, stored permuted in fragment order; the fp32 sums of every 32-value
-// sub-block (hi + lo fp16) are precomputed next to them for the K-quant
-// min-term MMA.  Scheduling is stream-K over the (row block, K-range) items:
-// the iteration space is split evenly over one or two CTAs per SM, a row block
-// split between CTAs being finished by its last contributor, which sums the
-// partials in CTA order (deterministic) from scratch memory.  Batch columns
-// that do not fit the resident budget are processed in groups by the caller.
-// Launches use programmatic dependent launch (griddepcontrol): a launch's
-// prologue, and with static weights its weight streaming, overlaps the tail
-// of the previous kernel on the stream.
+// The activations stay resident in shared memory for the whole CTA, stored
+// in the decode's fragment order, with the K-quant sub-block sums beside
+// them; one pass over X builds both.  The (row block, K-range) items are
+// split evenly over the CTAs; a row block cut between CTAs (at most the
+// first and the last of each CTA) is finished by its last contributor, which
+// sums the partials in CTA order from scratch memory.
 
 #include "gemv_q.cuh"
 
@@ -42,17 +39,11 @@
 namespace vkf {
 namespace gemv {
 
-constexpr int CW = 8;                 // consumer warps
-constexpr int NT = 32 * (CW + 1);
-constexpr int NST = 3;                // ring depth
-constexpr int ROW_BUDGET = 1600;      // max bytes of one row per item
-constexpr int X_BUDGET = 80 * 1024;   // resident activations + sums
+constexpr int NST_MAX = 8;            // ring depth cap
+constexpr int ROW_BUDGET = 4400;      // max bytes of one row per item
 constexpr int SMEM_MAX = 227 * 1024;
-// Two CTAs per SM when the activations are small: a CTA of the next launch
-// on the stream can then stream its weights while this one drains.
-constexpr int SMEM_HALF = 112 * 1024;
-constexpr int X_HALF = 36 * 1024;
-constexpr int ZERO_BYTES = 1024;      // zero activations / sums for columns >= M
+constexpr int X_BUDGET = 120 * 1024;  // resident activations + sums
+constexpr int MAX_SLOTS = NST_MAX + 2; // per-warp row-block partial slots
 
 struct Args {
     const uint8_t *W;
@@ -64,64 +55,124 @@ struct Args {
     int upi;           // units per item (the last item of a row block may have fewer)
     int S;             // items per row block
     int T;             // row blocks of 16 rows
-    int64_t I;         // T * S
+    int I;             // T * S
     int G;             // grid
+    int nst;           // ring depth
     int rpb;           // smem pitch of one row's bytes in a stage
-    int xpr;           // smem pitch of one resident activation row
-    int xsp;           // smem pitch of one column's sub-block sums
     int stage_bytes;
-    float *ws;         // partials: [G][2][128] floats
+    int xpr;           // smem pitch of one resident activation column
+    int xsp;           // smem pitch of one column's sub-block sums
+    int slots;         // partial slots (row blocks in flight)
+    int off_sums, off_ring, off_red, off_bar;
+    float *ws;         // partials of cut row blocks: [G][2][16 * M]
     int *cnt;          // per-row-block arrival counters (zero between launches)
     unsigned *err;
     int y_f16;
     int prefetch;      // stream weights before the previous kernel on the stream completes
-    int probe;         // debug (VKFLAME_GEMV_PROBE): 1 skips the decode (data path alone), 2 skips the
-                       // copies and waits (decode alone, on whatever the ring holds)
 };
 
-__device__ __forceinline__ int cta_of(int64_t i, const Args &a) { return (int)(((i + 1) * a.G - 1) / a.I); }
-__device__ __forceinline__ int64_t first_iter(int c, const Args &a) { return (int64_t)c * a.I / a.G; }
-__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory"); }
+__device__ __forceinline__ int first_item(int c, const Args &a) { return (int)((int64_t)c * a.I / a.G); }
+__device__ __forceinline__ int cta_of_item(int i, const Args &a) {
+    return (int)(((int64_t)(i + 1) * a.G - 1) / a.I);
+}
+template <int CW>
+__device__ __forceinline__ void consumer_bar() {
+    asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
+}
 
 __device__ __forceinline__ void store_y(const Args &a, int m, int n, float v) {
-    if (m < a.M && n < a.N) {
-        if (a.y_f16) reinterpret_cast<__half *>(a.Y)[(int64_t)m * a.ldy + n] = __float2half_rn(v);
-        else reinterpret_cast<float *>(a.Y)[(int64_t)m * a.ldy + n] = v;
+    if (a.y_f16) reinterpret_cast<__half *>(a.Y)[(int64_t)m * a.ldy + n] = __float2half_rn(v);
+    else reinterpret_cast<float *>(a.Y)[(int64_t)m * a.ldy + n] = v;
+}
+
+// Resident activations: one thread per (column, 32-value sub-block) reads the
+// 64 source bytes, stores them in fragment order (groups of four permuted
+// (x0, x2, x1, x3); owned layout: swizzled granules) and, for the K-quants,
+// their fp32 sum: split into hi + lo fp16 in the min-term MMA's B layout
+// [super-block][t] = (hi 2t, hi 2t+1, lo 2t, lo 2t+1), or (M = 1 column
+// form) as fp32 in the [super-block][t][2] order of the thread's sub-blocks.
+template <bool OWN, bool KQ, bool COLS, int NTC>
+__device__ __forceinline__ void load_activations(const Args &a, uint8_t *xs, uint8_t *sums) {
+    const int nsb = a.K / 32, jobs = a.M * nsb;
+    for (int j = threadIdx.x; j < jobs; j += NTC) {
+        const int m = j / nsb, sb = j - m * nsb;
+        const uint4 *src = reinterpret_cast<const uint4 *>(a.X + (int64_t)m * a.ldx_bytes + sb * 64);
+        uint4 v[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) v[c] = __ldg(src + c);
+        uint8_t *col = xs + m * a.xpr;
+        const int v0 = sb * 32;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t lo = w[2 * h], hi = w[2 * h + 1];  // values (x0 x1), (x2 x3)
+                const uint2 p = make_uint2(prmt(lo, hi, 0x5410), prmt(lo, hi, 0x7632));
+                const int v4 = v0 + 8 * c + 4 * h;  // first value of the group
+                const int off = OWN ? (v4 >> 8) * 512 + owned_group_offset(v4 & 255) : v4 * 2;
+                *reinterpret_cast<uint2 *>(col + off) = p;
+            }
+        }
+        if constexpr (KQ) {
+            float part[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+                float s2 = 0.f;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[e]));
+                    s2 += f.x + f.y;
+                }
+                part[c] = s2;
+            }
+            const float sum = (part[0] + part[1]) + (part[2] + part[3]);
+            if constexpr (COLS) {
+                reinterpret_cast<float *>(sums + m * a.xsp + (sb / 8) * 32)[m1_sum_slot(sb % 8)] = sum;
+                continue;
+            }
+            const __half hi = __float2half_rn(sum);
+            const __half lo = __float2half_rn(sum - __half2float(hi));
+            __half *o = reinterpret_cast<__half *>(sums + m * a.xsp + (sb / 8) * 32 + ((sb % 8) / 2) * 8) + (sb & 1);
+            o[0] = hi;
+            o[2] = lo;
+        }
     }
 }
 
-template <int QT>
-__global__ void __launch_bounds__(NT, 2) gemv_kernel(const __grid_constant__ Args a) {
-    constexpr int QK = Fmt<QT>::QK, BB = Fmt<QT>::BB, PARTS = Fmt<QT>::PARTS;
+template <int QT, int CW, bool M1>
+__global__ void __launch_bounds__(32 * (CW + 1), 1) gemv_kernel(const __grid_constant__ Args a) {
+    constexpr int NTC = 32 * CW;
+    constexpr int QK = Fmt<QT>::QK, BB = Fmt<QT>::BB;
     constexpr int UB = (256 / QK) * BB;  // bytes of one 256-value unit of a row
-    constexpr bool KQ = QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K;  // has a min term
+    constexpr bool KQ = QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K;
+    constexpr bool OWN = Step<QT>::OWNED;
+    constexpr bool COLS = M1 && KQ;  // sub-block-column decode (StepK1)
     extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t *xs = smem;                                       // M x xpr, permuted fp16
-    uint8_t *sums = xs + a.M * a.xpr;                         // M x xsp (K-quants)
-    uint8_t *zero = sums + a.M * a.xsp;                       // ZERO_BYTES of zeros
-    uint8_t *ring = zero + ZERO_BYTES;                        // NST x stage_bytes
-    uint64_t *full = reinterpret_cast<uint64_t *>(ring + NST * a.stage_bytes);
-    uint64_t *empty = full + NST;
-    int *redcnt = reinterpret_cast<int *>(empty + NST);       // NST + 1 arrival counters
-    float *red = reinterpret_cast<float *>(empty + NST + 2);  // (NST + 1) x CW x 32 x 4
+    uint8_t *xs = smem;
+    uint8_t *sums = smem + a.off_sums;
+    uint8_t *ring = smem + a.off_ring;
+    float *red = reinterpret_cast<float *>(smem + a.off_red);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + a.off_bar);
+    uint64_t *empty = full + NST_MAX;
+    int *slotcnt = reinterpret_cast<int *>(empty + NST_MAX);  // arrivals per reduction slot
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cta = blockIdx.x;
-    const int64_t it0 = first_iter(cta, a), it1 = first_iter(cta + 1, a);
-    // Programmatic dependent launch: let the next kernel on the stream start
+    const int it0 = first_item(cta, a), it1 = first_item(cta + 1, a);
+    // Programmatic dependent launch: the next kernel on the stream may start
     // its prologue now; everything this kernel reads or writes that another
     // kernel may touch (X, Y, the scratch) waits for the previous kernel.
     asm volatile("griddepcontrol.launch_dependents;");
-
-    for (int i = threadIdx.x; i < ZERO_BYTES / 16; i += NT) reinterpret_cast<uint4 *>(zero)[i] = make_uint4(0, 0, 0, 0);
     if (threadIdx.x == 0) {
-        for (int s = 0; s < NST; ++s) {
+        for (int s = 0; s < a.nst; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], CW);
         }
-        for (int r = 0; r <= NST; ++r) redcnt[r] = 0;
         fence_mbar_init();
     }
+    if (threadIdx.x < MAX_SLOTS) slotcnt[threadIdx.x] = 0;
     __syncthreads();
 
     if (warp == CW) {
@@ -129,20 +180,17 @@ __global__ void __launch_bounds__(NT, 2) gemv_kernel(const __grid_constant__ Arg
         // Weights that no kernel writes (a.prefetch) are streamed at once;
         // otherwise the producer too waits for the previous kernel.
         if (!a.prefetch) asm volatile("griddepcontrol.wait;" ::: "memory");
-        if (a.probe >= 2) return;
-        int n = 0;
-        for (int64_t it = it0; it < it1; ++it, ++n) {
-            const int s = n % NST;
-            const uint32_t ph = (uint32_t)(n / NST) & 1u;
-            if (n >= NST && !mbar_wait(&empty[s], ph ^ 1u, a.err)) break;
-            const int tile = (int)(it / a.S), step = (int)(it - (int64_t)tile * a.S);
+        int tile = it0 / a.S, step = it0 - tile * a.S, s = 0;
+        uint32_t ph = 0;
+        for (int it = it0, n = 0; it < it1; ++it, ++n) {
+            if (n >= a.nst && !mbar_wait(&empty[s], ph ^ 1u, a.err)) break;
             const int u0 = step * a.upi, nu = min(a.upi, a.units - u0);
             // Bytes of this item's units in one row (a partial last unit of a
             // 32-value-block format holds only the blocks that exist), widened
             // to whole 16-byte granules: a 16-byte aligned granule never
             // crosses a page, so the few bytes read either side are mapped.
             const int64_t b0 = (int64_t)u0 * UB;
-            const int64_t b1 = (int64_t)(u0 + nu) * UB < a.row_bytes ? (int64_t)(u0 + nu) * UB : a.row_bytes;
+            const int64_t b1 = min((int64_t)(u0 + nu) * UB, a.row_bytes);
             const int row = tile * 16 + lane;
             uint32_t sz = 0;
             const uint8_t *src = nullptr;
@@ -154,219 +202,230 @@ __global__ void __launch_bounds__(NT, 2) gemv_kernel(const __grid_constant__ Arg
             }
             uint32_t total = sz;
 #pragma unroll
-            for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+            for (int o = 8; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
             if (lane == 0) mbar_arrive_expect_tx(&full[s], total);
             __syncwarp();
             if (sz) bulk_g2s(ring + s * a.stage_bytes + lane * a.rpb, src, sz, &full[s]);
+            if (++step == a.S) {
+                step = 0;
+                ++tile;
+            }
+            if (++s == a.nst) {
+                s = 0;
+                ph ^= 1u;
+            }
         }
         return;
     }
 
     // ---------------- consumers ----------------
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // Resident activations, permuted (x0, x2, x1, x3) per group of four.
-    // Loads are batched through registers (read-only path) so their
-    // latencies overlap instead of serialising behind the shared stores.
-    {
-        const int groups = a.K / 4, total = a.M * groups;
-        constexpr int B = 8;
-        for (int i0 = threadIdx.x; i0 < total; i0 += B * CW * 32) {
-            uint2 v[B];
-#pragma unroll
-            for (int b = 0; b < B; ++b) {
-                const int i = i0 + b * CW * 32;
-                if (i < total) {
-                    const int m = i / groups, q = i - m * groups;
-                    v[b] = __ldg(reinterpret_cast<const uint2 *>(a.X + (int64_t)m * a.ldx_bytes) + q);
-                }
-            }
-#pragma unroll
-            for (int b = 0; b < B; ++b) {
-                const int i = i0 + b * CW * 32;
-                if (i < total) {
-                    const int m = i / groups, q = i - m * groups;
-                    *reinterpret_cast<uint2 *>(xs + m * a.xpr + q * 8) =
-                        make_uint2(prmt(v[b].x, v[b].y, 0x5410), prmt(v[b].x, v[b].y, 0x7632));
-                }
-            }
-        }
-    }
-    consumer_bar();
-    if constexpr (KQ) {
-        // fp32 sum of each 32-value sub-block, split hi + lo fp16, laid out as
-        // the min MMA's B fragment: [super-block][t] = (hi 2t, 2t+1 | lo 2t, 2t+1)
-        const int nsub = a.K / 32;
-        for (int i = threadIdx.x; i < a.M * nsub; i += CW * 32) {
-            const int m = i / nsub, j = i - m * nsub;
-            const uint4 *xr = reinterpret_cast<const uint4 *>(xs + m * a.xpr + j * 64);
-            float part[4];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const uint4 v = xr[c];
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-                float s2 = 0.f;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[e]));
-                    s2 += f.x + f.y;
-                }
-                part[c] = s2;
-            }
-            const float sum = (part[0] + part[1]) + (part[2] + part[3]);
-            const __half hi = __float2half_rn(sum);
-            const __half lo = __float2half_rn(sum - __half2float(hi));
-            __half *o = reinterpret_cast<__half *>(sums + m * a.xsp + (j / 8) * 32 + ((j % 8) / 2) * 8) + (j & 1);
-            o[0] = hi;
-            o[2] = lo;
-        }
-        consumer_bar();
-    }
+    load_activations<OWN, KQ, COLS, NTC>(a, xs, sums);
+    consumer_bar<CW>();
 
     const int g = lane >> 2, t = lane & 3;
-    const uint8_t *xg = g < a.M ? xs + g * a.xpr : nullptr;
-    const uint8_t *sg = g < a.M ? sums + g * a.xsp : nullptr;
+    // Lanes of columns >= M read a real column (their outputs are dropped),
+    // which keeps every fragment load a broadcast or conflict-free.
+    const int xcol = g % a.M;
+    const uint8_t *xg = xs + xcol * a.xpr;
+    const uint8_t *sg = sums + xcol * a.xsp;
+    const int rows16m = 16 * a.M;
     // After a bounded wait gives up (error bit already set) the warp keeps
-    // walking the same iterations without waiting or computing, so every
-    // consumer warp still reaches the same named barriers.
+    // walking the same items without waiting or computing, so every consumer
+    // warp still reaches the same barriers.
     bool ok = true;
-    float acc[4];
-    zero4(acc);
-    const int first_tile = (int)(it0 / a.S);
-    // Warps take the units of the CTA's item sequence round-robin (unit i of
-    // the sequence goes to warp i mod CW), never waiting for each other: a
-    // warp releases a ring slot when done with it, and at the end of a row
-    // block leaves its partial in one of NST + 1 reduction buffers (a warp
-    // can run at most NST items ahead); the last warp to arrive reduces.
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    int tile = it0 / a.S, step = it0 - tile * a.S, s = 0;
+    uint32_t ph = 0;
     int ubase = 0;  // units of this CTA's earlier items, mod CW
-    int tiles_done = 0;
-    int n = 0;
-    for (int64_t it = it0; it < it1; ++it, ++n) {
-        const int s = n % NST;
-        const uint32_t ph = (uint32_t)(n / NST) & 1u;
-        if (ok && a.probe < 2) ok = mbar_wait(&full[s], ph, a.err);
-        const int tile = (int)(it / a.S), step = (int)(it - (int64_t)tile * a.S);
+    int slot = 0, done_tile = tile;
+    const int first_tile = tile;
+    for (int it = it0; it < it1; ++it) {
+        if (ok) ok = mbar_wait(&full[s], ph, a.err);
         const int u0 = step * a.upi, nu = min(a.upi, a.units - u0);
-        if (ok && (a.probe == 0 || a.probe == 2)) {
+        if (ok) {
             const uint8_t *st = ring + s * a.stage_bytes;
-            const int64_t row_a = (int64_t)tile * 16 + g, row_b = row_a + 8;
+            const int64_t row_a = (int64_t)tile * 16 + g;
             const uintptr_t ga = (uintptr_t)a.W + row_a * a.row_bytes + (int64_t)u0 * UB;
-            const uintptr_t gb = (uintptr_t)a.W + row_b * a.row_bytes + (int64_t)u0 * UB;
+            const uintptr_t gb = ga + 8 * a.row_bytes;
             const uint8_t *ra = st + g * a.rpb + (ga & 15), *rb = st + (g + 8) * a.rpb + (gb & 15);
             int u = warp - ubase;
             if (u < 0) u += CW;
             for (; u < nu; u += CW) {
-                const int kv = (u0 + u) * 256;
-                const int nblk = min(8, (a.K - kv) / 32);
-                const uint8_t *xc = xg ? xg + kv * 2 : zero;
-                const uint8_t *xsum = sg ? sg + (u0 + u) * 32 : zero;
-                Step<QT>::run(ra + u * UB, rb + u * UB, xc, xsum, t, 0, nblk, acc);
+                const int unit = u0 + u;
+                if constexpr (COLS) {
+                    StepK1<QT == VKF_DEQUANT_Q5_K>::run(ra + u * UB, rb + u * UB, xs + unit * 512, g == t, g == t + 4,
+                                                        reinterpret_cast<const float *>(sums + unit * 32), t, acc);
+                } else {
+                    const int nblk = QK == 32 ? min(8, (a.K - unit * 256) / 32) : 8;
+                    Step<QT>::run(ra + u * UB, rb + u * UB, xg + unit * 512, sg + unit * 32, t, nblk, acc);
+                }
             }
         }
-        ubase = (ubase + nu) % CW;
+        ubase += nu;
+        while (ubase >= CW) ubase -= CW;
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == a.nst) {
+            s = 0;
+            ph ^= 1u;
+        }
+        const bool tile_end = step == a.S - 1 || it + 1 == it1;
+        if (++step == a.S) {
+            step = 0;
+            ++tile;
+        }
+        if (!tile_end) continue;
 
-        if (step != a.S - 1 && it + 1 != it1) continue;
-
-        // ---- row-block epilogue: the last warp to arrive reduces ----
-        const int rbuf = tiles_done % (NST + 1);
-        ++tiles_done;
-        float *rbase = red + rbuf * CW * 128;
-        reinterpret_cast<float4 *>(rbase)[warp * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        zero4(acc);
-        __threadfence_block();
+        if constexpr (COLS) StepK1<QT == VKF_DEQUANT_Q5_K>::finish(acc);
+        // Park this warp's partial of the finished row block in the block's
+        // slot; the last warp to arrive reduces the slot in warp order
+        // (deterministic) while the others go on decoding.  A warp runs at
+        // most nst items ahead of the slowest, so nst + 2 slots never alias.
+        float *p = red + (slot * CW + warp) * rows16m;
+        {
+            const int c0 = 2 * t, c1 = 2 * t + 1;
+            if (c0 < a.M) {
+                p[g * a.M + c0] = acc[0];
+                p[(g + 8) * a.M + c0] = acc[2];
+            }
+            if (c1 < a.M) {
+                p[g * a.M + c1] = acc[1];
+                p[(g + 8) * a.M + c1] = acc[3];
+            }
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+        }
+        const int tb = done_tile, sl = slot;
+        ++done_tile;
+        if (++slot == a.slots) slot = 0;
         __syncwarp();
         int last = 0;
-        if (lane == 0) last = atomicAdd(&redcnt[rbuf], 1) == CW - 1;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) continue;
-        __threadfence_block();
-        float o[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int w = 0; w < CW; ++w) {
-            const float4 v = reinterpret_cast<const float4 *>(rbase)[w * 32 + lane];
-            o[0] += v.x;
-            o[1] += v.y;
-            o[2] += v.z;
-            o[3] += v.w;
+        if (lane == 0) {
+            __threadfence_block();
+            last = atomicAdd(&slotcnt[sl], 1) == CW - 1;
+            if (last) __threadfence_block();
         }
-        __syncwarp();
-        if (lane == 0) redcnt[rbuf] = 0;
-        const int64_t tb = (int64_t)tile * a.S;
-        const bool whole = tb >= it0 && tb + a.S <= it1;
-        bool write = true;
-        if (!whole) {
-            const int slot = tile == first_tile ? 0 : 1;
-            reinterpret_cast<float4 *>(a.ws + ((int64_t)cta * 2 + slot) * 128)[lane] = make_float4(o[0], o[1], o[2], o[3]);
-            __threadfence();
-            __syncwarp();
-            const int c_first = cta_of(tb, a), c_last = cta_of(tb + a.S - 1, a);
-            int fin = 0;
-            if (lane == 0) fin = atomicAdd(&a.cnt[tile], 1) == c_last - c_first;
-            fin = __shfl_sync(0xffffffffu, fin, 0);
-            write = fin != 0;
-            if (write) {
-                __threadfence();
-                zero4(o);
+        if (!__shfl_sync(0xffffffffu, last, 0)) continue;
+
+        const float *q = red + sl * CW * rows16m;
+        const bool whole = tb * a.S >= it0 && (tb + 1) * a.S <= it1;
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int rc = lane + 32 * j;
+            o[j] = 0.f;
+            if (rc < rows16m) {
 #pragma unroll 4
-                for (int c = c_first; c <= c_last; ++c) {
-                    const int cslot = (tile == (int)(first_iter(c, a) / a.S)) ? 0 : 1;
-                    const float4 v =
-                        __ldcg(reinterpret_cast<const float4 *>(a.ws + ((int64_t)c * 2 + cslot) * 128) + lane);
-                    o[0] += v.x;
-                    o[1] += v.y;
-                    o[2] += v.z;
-                    o[3] += v.w;
-                }
-                if (lane == 0) atomicExch(&a.cnt[tile], 0);
+                for (int w = 0; w < CW; ++w) o[j] += q[w * rows16m + rc];
             }
         }
-        if (write) {
-            const int row = tile * 16 + g;
-            store_y(a, 2 * t, row, o[0]);
-            store_y(a, 2 * t + 1, row, o[1]);
-            store_y(a, 2 * t, row + 8, o[2]);
-            store_y(a, 2 * t + 1, row + 8, o[3]);
+        __syncwarp();
+        if (lane == 0) slotcnt[sl] = 0;
+        if (whole) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int rc = lane + 32 * j, r = rc / a.M, c = rc - r * a.M;
+                if (rc < rows16m && tb * 16 + r < a.N) store_y(a, c, tb * 16 + r, o[j]);
+            }
+            continue;
         }
+        // A row block cut between CTAs: publish this CTA's partial; the last
+        // contributor to arrive sums all partials in CTA order and stores Y.
+        const int which = tb == first_tile ? 0 : 1;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int rc = lane + 32 * j;
+            if (rc < rows16m) a.ws[((int64_t)cta * 2 + which) * rows16m + rc] = o[j];
+        }
+        const int c_first = cta_of_item(tb * a.S, a), c_last = cta_of_item((tb + 1) * a.S - 1, a);
+        __syncwarp();
+        int fin = 0;
+        if (lane == 0) {
+            __threadfence();
+            fin = atomicAdd(&a.cnt[tb], 1) == c_last - c_first;
+            if (fin) __threadfence();
+        }
+        if (!__shfl_sync(0xffffffffu, fin, 0)) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int rc = lane + 32 * j;
+            if (rc >= rows16m) continue;
+            float v = 0.f;
+            for (int c = c_first; c <= c_last; ++c) {
+                const int wc = tb == first_item(c, a) / a.S ? 0 : 1;
+                v += __ldcg(a.ws + ((int64_t)c * 2 + wc) * rows16m + rc);
+            }
+            const int r = rc / a.M, col = rc - r * a.M;
+            if (tb * 16 + r < a.N) store_y(a, col, tb * 16 + r, v);
+        }
+        if (lane == 0) a.cnt[tb] = 0;
     }
 }
 
-template <int QT>
+template <int QT, int CW, bool M1>
 struct Launcher {
     static constexpr int QK = Fmt<QT>::QK, BB = Fmt<QT>::BB;
     static constexpr int UB = (256 / QK) * BB;
     static constexpr bool KQ = QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K;
+    static constexpr bool OWN = Step<QT>::OWNED;
+    static constexpr int NT = 32 * (CW + 1);
+
     static int launch(Args &a, int sms, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap) {
+        auto up = [](int64_t v, int64_t m) { return (v + m - 1) / m * m; };
         a.units = (a.K + 255) / 256;
-        a.xpr = ((a.K * 2 + 95) / 128) * 128 + 32;  // pitch = 8 banks mod 32: conflict-free fragment loads
-        a.xsp = KQ ? ((a.K / 256) * 32 + 15) / 16 * 16 : 0;
-        const int fixed = a.M * (a.xpr + a.xsp) + ZERO_BYTES + 2 * NST * 8 + 16 + (NST + 1) * CW * 32 * 16;
-        const int budget = a.M * (a.xpr + a.xsp) <= X_HALF ? SMEM_HALF : SMEM_MAX;
-        const int row_avail = (budget - fixed) / (NST * 16) - 32;  // room for padding and misalignment
-        const int umax = std::min(ROW_BUDGET, row_avail) / UB;
-        if (umax < 1) return VKF_ERR_UNSUPPORTED;
-        a.S = (a.units + umax - 1) / umax;
-        a.upi = (a.units + a.S - 1) / a.S;
-        a.S = (a.units + a.upi - 1) / a.upi;
+        // Column pitches: the owned layout's 16-byte fragment loads want
+        // columns 64 bytes apart mod 128 banks-wise, the plain layout's
+        // 8-byte loads 32 bytes.
+        a.xpr = (int)up((int64_t)a.units * 512, 128) + (OWN ? 64 : 32);
+        a.xsp = KQ ? (int)up((int64_t)a.units * 32, 16) : 0;
+        a.off_sums = a.M * a.xpr;
+        const int x_end = (int)up(a.off_sums + (int64_t)a.M * a.xsp, 128);
+        if (x_end > X_BUDGET) return VKF_ERR_UNSUPPORTED;
+        const int rows16m = 16 * a.M;
+        const int slot_bytes = CW * rows16m * 4;
+        const int bar_bytes = 2 * NST_MAX * 8 + MAX_SLOTS * 4;
+        const int avail = SMEM_MAX - x_end - bar_bytes - 128;
         a.T = (a.N + 15) / 16;
-        a.I = (int64_t)a.T * a.S;
-        const int ng = ((a.upi * UB + 15) / 16 + 1) | 1;  // odd granule count: rows 4 banks apart
-        a.rpb = ng * 16;
-        a.stage_bytes = 16 * a.rpb;
-        const size_t smem = (size_t)fixed + NST * (size_t)a.stage_bytes;
-        if (smem > (size_t)budget) return VKF_ERR_UNSUPPORTED;
+
+        // Units per item: whole rows when a row fits the budget (a 16-row
+        // item is then one contiguous range of the matrix, which DRAM streams
+        // at full rate; K-ranges of ~1.5 KB per row measured ~40% slower), a
+        // K-split only as far as the row length requires.  A short N (fewer
+        // row blocks than SMs) is not split further: the cross-CTA fixups of
+        // cut row blocks cost more than the idle SMs (measured).
+        const int upi_max = std::max(1, std::min(a.units, ROW_BUDGET / UB));
+        a.S = (a.units + upi_max - 1) / upi_max;
+        a.upi = (a.units + a.S - 1) / a.S;
+        for (;;) {
+            const int ng = ((a.upi * UB + 15) / 16 + 1) | 1;  // odd granule count: rows 16 banks apart
+            a.rpb = ng * 16;
+            a.stage_bytes = 16 * a.rpb;
+            a.nst = std::min(NST_MAX, (avail - 2 * slot_bytes) / (a.stage_bytes + slot_bytes));
+            if (a.nst >= 2 || a.upi == 1) break;
+            a.upi = std::max(1, a.upi / 2);
+            a.S = (a.units + a.upi - 1) / a.upi;
+            a.upi = (a.units + a.S - 1) / a.S;
+        }
+        if (a.nst < 2) return VKF_ERR_UNSUPPORTED;
+        if ((int64_t)a.T * a.S > (int64_t)1 << 30) return VKF_ERR_UNSUPPORTED;
+        a.I = a.T * a.S;
+        a.slots = a.nst + 2;
+        const int red_bytes = (int)up((int64_t)a.slots * slot_bytes, 128);
+        a.off_ring = x_end;
+        a.off_red = a.off_ring + a.nst * a.stage_bytes;
+        a.off_bar = a.off_red + red_bytes;
+        const size_t smem = (size_t)a.off_bar + bar_bytes;
         static bool attr_set[64] = {false};
         int dev = 0;
         cudaGetDevice(&dev);
         if (dev < 64 && !attr_set[dev]) {
-            cudaFuncSetAttribute(gemv_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX);
+            cudaFuncSetAttribute(gemv_kernel<QT, CW, M1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX);
             attr_set[dev] = true;
         }
-        a.G = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)sms * (budget == SMEM_HALF ? 2 : 1), a.I));
-        if ((size_t)a.G * 2 * 128 > ws_cap || (size_t)a.T > cnt_cap) return VKF_ERR_INVALID;
+        a.G = std::max(1, std::min(sms, a.I));
+        if ((size_t)a.G * 2 * rows16m > ws_cap || (size_t)a.T > cnt_cap) return VKF_ERR_INVALID;
         a.ws = ws;
         a.cnt = cnt;
-        static const int probe = [] { const char *e = getenv("VKFLAME_GEMV_PROBE"); return e ? atoi(e) : 0; }();
-        a.probe = probe;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(a.G);
         cfg.blockDim = dim3(NT);
@@ -377,27 +436,47 @@ struct Launcher {
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        cudaLaunchKernelEx(&cfg, gemv_kernel<QT>, a);
+        cudaLaunchKernelEx(&cfg, gemv_kernel<QT, CW, M1>, a);
         return check_launch();
     }
 };
+
+// 8 consumer warps: with 16, each warp decodes fewer units per item and the
+// per-item overhead grows faster than the latency hiding gains (measured).
+constexpr int CW_DEFAULT = 8;
+
+template <int QT>
+static int launch_q(Args &a, int sms, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap) {
+    constexpr bool KQ = QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K;
+    if (KQ && a.M == 1) return Launcher<QT, CW_DEFAULT, true>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    return Launcher<QT, CW_DEFAULT, false>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+}
+
+static int dispatch(int wtype, Args &a, int sms, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt,
+                    size_t cnt_cap) {
+    switch (wtype) {
+    case VKF_DEQUANT_Q4_0: return launch_q<VKF_DEQUANT_Q4_0>(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    case VKF_DEQUANT_Q8_0: return launch_q<VKF_DEQUANT_Q8_0>(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    case VKF_DEQUANT_Q4_K: return launch_q<VKF_DEQUANT_Q4_K>(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    case VKF_DEQUANT_Q5_K: return launch_q<VKF_DEQUANT_Q5_K>(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    case VKF_DEQUANT_Q6_K: return launch_q<VKF_DEQUANT_Q6_K>(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    default: return VKF_ERR_UNSUPPORTED;
+    }
+}
 
 }  // namespace gemv
 
 // Batch columns per launch so the resident activations fit the budget.
 int gemv_cols_per_launch(int K) {
-    const size_t per = (size_t)K * 2 + 160 + (size_t)K / 8;
-    return (int)std::max<size_t>(1, std::min<size_t>(8, gemv::X_BUDGET / per));
+    const size_t units = ((size_t)K + 255) / 256;
+    const size_t per = (units * 512 + 127) / 128 * 128 + 64 + units * 32;
+    return (int)std::max<size_t>(1, std::min<size_t>(8, (gemv::X_BUDGET - 128) / per));
 }
 size_t gemv_counters(int N) { return (size_t)(N + 15) / 16; }
-size_t gemv_ws_floats(int sms) { return (size_t)sms * 2 * 2 * 128; }
+size_t gemv_ws_floats(int sms) { return (size_t)sms * 2 * 16 * 8; }
 
-// X: fp16, rows 16-byte aligned (ldx_bytes multiple of 16).  Checked by caller.
-int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void *Y, int y_f16, int64_t ldy, int M,
-                int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap, int prefetch) {
-    DeviceState *ds = device_state();
-    if (!ds) return VKF_ERR_NO_DEVICE;
-    gemv::Args a{};
+static void fill_args(gemv::Args &a, int wtype, const void *W, const void *X, int64_t ldx_bytes, void *Y, int y_f16,
+                      int64_t ldy, int M, int N, int K) {
     a.W = (const uint8_t *)W;
     a.X = (const uint8_t *)X;
     a.Y = Y;
@@ -407,18 +486,19 @@ int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void
     a.ldx_bytes = ldx_bytes;
     a.ldy = ldy;
     a.row_bytes = (int64_t)K / vkf_qtype_block_values(wtype) * vkf_qtype_block_bytes(wtype);
-    a.err = ds->d_error;
     a.y_f16 = y_f16;
+}
+
+// X: fp16, rows 16-byte aligned (ldx_bytes multiple of 16).  Checked by caller.
+int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void *Y, int y_f16, int64_t ldy, int M,
+                int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap, int prefetch) {
+    DeviceState *ds = device_state();
+    if (!ds) return VKF_ERR_NO_DEVICE;
+    gemv::Args a{};
+    fill_args(a, wtype, W, X, ldx_bytes, Y, y_f16, ldy, M, N, K);
+    a.err = ds->d_error;
     a.prefetch = prefetch;
-    const int sms = ds->sm_count;
-    switch (wtype) {
-    case VKF_DEQUANT_Q4_0: return gemv::Launcher<VKF_DEQUANT_Q4_0>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    case VKF_DEQUANT_Q8_0: return gemv::Launcher<VKF_DEQUANT_Q8_0>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    case VKF_DEQUANT_Q4_K: return gemv::Launcher<VKF_DEQUANT_Q4_K>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    case VKF_DEQUANT_Q5_K: return gemv::Launcher<VKF_DEQUANT_Q5_K>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    case VKF_DEQUANT_Q6_K: return gemv::Launcher<VKF_DEQUANT_Q6_K>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    default: return VKF_ERR_UNSUPPORTED;
-    }
+    return gemv::dispatch(wtype, a, ds->sm_count, stream, ws, ws_cap, cnt, cnt_cap);
 }
 
 // Same launch with the SM count and the kernel error word supplied by the
@@ -428,26 +508,10 @@ int gemv_launch_raw(int wtype, const void *W, const void *X, int64_t ldx_bytes, 
                     int M, int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap,
                     int sms, unsigned *err) {
     gemv::Args a{};
-    a.W = (const uint8_t *)W;
-    a.X = (const uint8_t *)X;
-    a.Y = Y;
-    a.M = M;
-    a.N = N;
-    a.K = K;
-    a.ldx_bytes = ldx_bytes;
-    a.ldy = ldy;
-    a.row_bytes = (int64_t)K / vkf_qtype_block_values(wtype) * vkf_qtype_block_bytes(wtype);
+    fill_args(a, wtype, W, X, ldx_bytes, Y, y_f16, ldy, M, N, K);
     a.err = err;
-    a.y_f16 = y_f16;
     a.prefetch = 0;
-    switch (wtype) {
-    case VKF_DEQUANT_Q4_0: return gemv::Launcher<VKF_DEQUANT_Q4_0>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    case VKF_DEQUANT_Q8_0: return gemv::Launcher<VKF_DEQUANT_Q8_0>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    case VKF_DEQUANT_Q4_K: return gemv::Launcher<VKF_DEQUANT_Q4_K>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    case VKF_DEQUANT_Q5_K: return gemv::Launcher<VKF_DEQUANT_Q5_K>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    case VKF_DEQUANT_Q6_K: return gemv::Launcher<VKF_DEQUANT_Q6_K>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    default: return VKF_ERR_UNSUPPORTED;
-    }
+    return gemv::dispatch(wtype, a, sms, stream, ws, ws_cap, cnt, cnt_cap);
 }
 
 }  // namespace vkf

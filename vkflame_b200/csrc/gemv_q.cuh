@@ -1,18 +1,28 @@
-// gemv_q.cuh — per-format decode of one work unit of a 16-row group into
+// gemv_q.cuh — per-format decode of one 256-value unit of a 16-row group into
 // m16n8k16 tensor-core fragments, for the decode GEMV (M <= 8).
 //
-// Fragment mapping.  The 16 k-slots of each MMA cover 16 consecutive values
-// of one 32-value (sub-)block; thread t (= lane & 3) owns the 4 values
-// 4t..4t+3, so its weight bytes are one 32-bit word.  Within the MMA, slot
-// (2t, 2t+1) holds values (4t, 4t+2) and slot (2t+8, 2t+9) holds (4t+1, 4t+3):
-// exactly the half2 pairs a single LOP3 extracts from bytes (0,2) and (1,3)
-// of the word.  The activations (B fragment) are stored with the same
-// permutation, so the dot product is unchanged.
+// A = 16 weight rows (thread (g, t) = (lane >> 2, lane & 3) holds rows g and
+// g + 8), B = the M <= 8 activation columns, fp32 accumulators.  Every MMA's
+// 16 k-slots may hold any 16 values of the unit as long as the activation
+// fragment holds the matching values; two assignments are used:
+//
+//   plain   (Q4_0, Q8_0, Q6_K): the 16 slots cover 16 consecutive values;
+//           thread t owns values 4t..4t+3, one 32-bit word of weight bytes.
+//           Slots (2t, 2t+1) hold values (4t, 4t+2) and (2t+8, 2t+9) hold
+//           (4t+1, 4t+3): the half2 pairs one LOP3 extracts from bytes (0,2)
+//           and (1,3) of the word.  Activations are stored (x0, x2, x1, x3)
+//           per group of four, so a fragment is one 64-bit load.
+//   owned   (Q4_K, Q5_K): thread t owns the 32 quant bytes 32t..32t+31 of
+//           the super-block, i.e. sub-blocks 2t (low nibbles) and 2t+1 (high
+//           nibbles) of dequant_q4_k.glsl:41-57, read as two 16-byte loads;
+//           it needs only its own two 6-bit scales and mins.  The activation
+//           groups of four are stored with a 16-byte-granule XOR swizzle so
+//           that the four threads' 16-byte fragment loads hit distinct banks.
 //
 // Exactness.  The A operand is always an integer that fp16 represents
 // exactly: q-8 (Q4_0), q (Q8_0), sc*q (Q4_K, <= 945; Q5_K, <= 1953), q-32
 // (Q6_K), m (K-quant mins).  They are produced from "1024 + code" fp16 bit
-// patterns with one fp16 operation whose exact result is that integer, so the
+// patterns with one fp16 FMA whose exact result is that integer, so its
 // single rounding is exact.  Products with fp16 activations are exact in the
 // fp32 accumulator; the per-block fp32 scales (d, d*sc, dmin) are applied to
 // the fp32 partial sums.  The only roundings are fp32 accumulation (and the
@@ -24,14 +34,14 @@
 namespace vkf {
 namespace gemv {
 
-// QK values per block, BB bytes per block, PARTS work units per 256 values
-// (1: a warp decodes whole super-blocks / 8-block groups).
+// QK values per block, BB bytes per block.  A work unit is 256 values of a
+// row: one super-block, or eight 32-value blocks.
 template <int QT> struct Fmt;
-template <> struct Fmt<VKF_DEQUANT_Q4_0> { static constexpr int QK = 32, BB = 18, PARTS = 1; };
-template <> struct Fmt<VKF_DEQUANT_Q8_0> { static constexpr int QK = 32, BB = 34, PARTS = 1; };
-template <> struct Fmt<VKF_DEQUANT_Q4_K> { static constexpr int QK = 256, BB = 144, PARTS = 1; };
-template <> struct Fmt<VKF_DEQUANT_Q5_K> { static constexpr int QK = 256, BB = 176, PARTS = 1; };
-template <> struct Fmt<VKF_DEQUANT_Q6_K> { static constexpr int QK = 256, BB = 210, PARTS = 1; };
+template <> struct Fmt<VKF_DEQUANT_Q4_0> { static constexpr int QK = 32, BB = 18; };
+template <> struct Fmt<VKF_DEQUANT_Q8_0> { static constexpr int QK = 32, BB = 34; };
+template <> struct Fmt<VKF_DEQUANT_Q4_K> { static constexpr int QK = 256, BB = 144; };
+template <> struct Fmt<VKF_DEQUANT_Q5_K> { static constexpr int QK = 256, BB = 176; };
+template <> struct Fmt<VKF_DEQUANT_Q6_K> { static constexpr int QK = 256, BB = 210; };
 
 // fp16 constants (bit patterns)
 constexpr uint32_t H2_MAGIC = 0x64006400u;  // (1024, 1024)
@@ -76,8 +86,9 @@ __device__ __forceinline__ void zero4(float (&p)[4]) { p[0] = p[1] = p[2] = p[3]
 template <int QT> struct Step;
 
 template <> struct Step<VKF_DEQUANT_Q4_0> {
+    static constexpr bool OWNED = false;
     __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
-                                               const uint8_t *, int t, int, int nblk, float (&acc)[4]) {
+                                               const uint8_t *, int t, int nblk, float (&acc)[4]) {
 #pragma unroll 8
         for (int c = 0; c < 8; ++c) {
             if (c >= nblk) break;
@@ -110,8 +121,9 @@ template <> struct Step<VKF_DEQUANT_Q4_0> {
 };
 
 template <> struct Step<VKF_DEQUANT_Q8_0> {
+    static constexpr bool OWNED = false;
     __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
-                                               const uint8_t *, int t, int, int nblk, float (&acc)[4]) {
+                                               const uint8_t *, int t, int nblk, float (&acc)[4]) {
 #pragma unroll 8
         for (int c = 0; c < 8; ++c) {
             if (c >= nblk) break;
@@ -139,116 +151,241 @@ template <> struct Step<VKF_DEQUANT_Q8_0> {
     }
 };
 
-// [code, 0x64, code, 0x64] from byte `idx` of w: half2 (1024+code, 1024+code).
-__device__ __forceinline__ uint32_t dup_byte_magic(uint32_t w, int idx) {
-    return prmt(w, 0x64646464u, (uint32_t)(idx * 0x101 + 0x4040));
+__device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+
+// Byte offset, within one column's 512-byte super-block block of the owned
+// activation layout, of the fragment group holding value v (0..255): groups
+// of four values (x0, x2, x1, x3), two groups per 16-byte granule, granule
+// j = v / 8 stored at j ^ ((j / 8) & 3).
+__host__ __device__ __forceinline__ int owned_group_offset(int v) {
+    const int q = v >> 2, j = q >> 1;
+    return ((j ^ ((j >> 3) & 3)) << 4) + ((q & 1) << 3);
 }
 
-// Unpacked 6-bit scales/mins of a K-quant super-block, four per word:
-// sc[0..3], sc[4..7], m[0..3], m[4..7] (get_scale_min_k4, dequant_q4_k.glsl:16-24).
-struct KScales {
-    uint32_t scA, scB, mA, mB;
-    __device__ __forceinline__ explicit KScales(const uint8_t *s) {
-        uint32_t s0 = ld32(s), s1 = ld32(s + 4), s2 = ld32(s + 8);
-        scA = s0 & 0x3F3F3F3Fu;
-        mA = s1 & 0x3F3F3F3Fu;
-        scB = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
-        mB = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
+// Per-thread constants of one K-quant row for the thread's sub-blocks 2t and
+// 2t+1 (get_scale_min_k4, dequant_q4_k.glsl:16-24), from the 16-byte header
+// [d, dmin, scales[12]]:
+//   sl, cl:  (sc_2t, sc_2t) and -1024 * sc_2t   (low nibbles: (1024+q)*sc - 1024*sc)
+//   sh, ch:  sc_2t+1 / 16 and -64 * sc_2t+1     (high nibbles: (1024+16q)*sc/16 - 64*sc)
+//   am:      (m_2t, m_2t+1)                     (min-term MMA operand)
+struct KRow {
+    uint32_t sl, cl, sh, ch, am;
+    float d, dm;
+    __device__ __forceinline__ KRow(const uint4 h, int t) {
+        const uint32_t scA = h.y & 0x3F3F3F3Fu, mA = h.z & 0x3F3F3F3Fu;
+        const uint32_t scB = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+        const uint32_t mB = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+        const uint32_t scw = t < 2 ? scA : scB, mw = t < 2 ? mA : mB;
+        const uint32_t b = (uint32_t)(t & 1) * 2;  // byte of sub-block 2t in its word
+        const uint32_t sel = b * 0x0101u + 0x4040u;  // [byte b, 0x64, byte b, 0x64]
+        const uint32_t lo = hsub2_u(prmt(scw, 0x64646464u, sel), H2_1024);
+        const uint32_t hi = hsub2_u(prmt(scw, 0x64646464u, sel + 0x0101u), H2_1024);
+        sl = lo;
+        cl = hmul2_u(lo, H2_M1024);
+        sh = hmul2_u(hi, H2_SIXTEENTH);
+        ch = hmul2_u(hi, H2_M64);
+        am = hsub2_u(prmt(mw, 0x64646464u, b + 0x4040u + (b + 1) * 0x100u), H2_1024);
+        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&h.x));
+        d = f.x;
+        dm = f.y;
     }
-    __device__ __forceinline__ uint32_t sc(int j) const { return hsub2_u(dup_byte_magic(j < 4 ? scA : scB, j & 3), H2_1024); }
-    __device__ __forceinline__ uint32_t mn(int j) const { return hsub2_u(dup_byte_magic(j < 4 ? mA : mB, j & 3), H2_1024); }
 };
 
-// Q4_K and Q5_K (dequant_q4_k.glsl / dequant_q5_k.glsl): value = (d*sc)*q - dmin*m.
-// A operand = sc*q (exact).  The min term sum_j m_j * X_j, X_j the sum of
-// the activations over sub-block j, is one extra MMA per super-block whose
-// k-slots are the 8 sub-blocks: A = m_j, B = X_j split into fp16 hi (slots
-// 0..7) + lo (slots 8..15), precomputed once per CTA.  Each call decodes a
-// range of 64-value chunks [IL0, IL0 + NIL); IL0 == 0 also does the min MMA.
-template <bool Q5, int IL0, int NIL> struct StepK {
+// Q4_K and Q5_K (dequant_q4_k.glsl / dequant_q5_k.glsl): value = (d*sc)*q - dmin*m,
+// owned mapping.  MMA pair i (i = 0..7) takes quant word i of the thread's
+// chunk: its low nibbles (bytes 0,2 | 1,3) form the sub-block-2t MMA, its high
+// nibbles the sub-block-2t+1 MMA; A = sc*q (exact).  Q5_K ORs the fifth bit
+// qh[l] bit 2t / 2t+1 (dequant_q5_k.glsl:52-69) into the codes first.  The min
+// term sum_j m_j * X_j (X_j the activation sum over sub-block j) is one MMA:
+// thread t's k-slots hold m_2t, m_2t+1 against X_2t, X_2t+1 split into fp16
+// hi (slots 2t, 2t+1) + lo (slots 2t+8, 2t+9), precomputed once per CTA.
+template <bool Q5> struct StepK {
+    static constexpr bool OWNED = true;
     __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
-                                               const uint8_t *xs, int t, float (&acc)[4]) {
+                                               const uint8_t *xs, int t, int, float (&acc)[4]) {
         constexpr int QS = Q5 ? 48 : 16;
-        const float da = hbits(ra), db = hbits(rb);
-        KScales ka(ra + 4), kb(rb + 4);
-        float p1[2][4];
-        zero4(p1[0]);
-        zero4(p1[1]);
+        const KRow ka(lds128(ra), t), kb(lds128(rb), t);
+        uint32_t wa[8], wb[8];
+        {
+            const uint4 a0 = lds128(ra + QS + 32 * t), a1 = lds128(ra + QS + 16 + 32 * t);
+            const uint4 b0 = lds128(rb + QS + 32 * t), b1 = lds128(rb + QS + 16 + 32 * t);
+            wa[0] = a0.x; wa[1] = a0.y; wa[2] = a0.z; wa[3] = a0.w; wa[4] = a1.x; wa[5] = a1.y; wa[6] = a1.z; wa[7] = a1.w;
+            wb[0] = b0.x; wb[1] = b0.y; wb[2] = b0.z; wb[3] = b0.w; wb[4] = b1.x; wb[5] = b1.y; wb[6] = b1.z; wb[7] = b1.w;
+        }
+        uint32_t ha[8], hb[8];
+        if constexpr (Q5) {
+            const uint4 a0 = lds128(ra + 16), a1 = lds128(ra + 32), b0 = lds128(rb + 16), b1 = lds128(rb + 32);
+            ha[0] = a0.x; ha[1] = a0.y; ha[2] = a0.z; ha[3] = a0.w; ha[4] = a1.x; ha[5] = a1.y; ha[6] = a1.z; ha[7] = a1.w;
+            hb[0] = b0.x; hb[1] = b0.y; hb[2] = b0.z; hb[3] = b0.w; hb[4] = b1.x; hb[5] = b1.y; hb[6] = b1.z; hb[7] = b1.w;
+        }
+        float p0[4] = {0.f, 0.f, 0.f, 0.f}, p1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int i = 0; i < NIL; ++i) {
-            const int il = IL0 + i;
-            const int j0 = 2 * il, j1 = 2 * il + 1;
-            uint32_t sla = ka.sc(j0), slb = kb.sc(j0);
-            uint32_t cla = hmul2_u(sla, H2_M1024), clb = hmul2_u(slb, H2_M1024);
-            uint32_t sha = ka.sc(j1), shb = kb.sc(j1);
-            uint32_t cha = hmul2_u(sha, H2_M64), chb = hmul2_u(shb, H2_M64);
-            sha = hmul2_u(sha, H2_SIXTEENTH);
-            shb = hmul2_u(shb, H2_SIXTEENTH);
+        for (int i = 0; i < 8; i += 2) {
+            const uint4 xl = lds128(xc + owned_group_offset(64 * t + 4 * i));
+            const uint4 xh = lds128(xc + owned_group_offset(64 * t + 32 + 4 * i));
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                uint32_t wa = ld32(ra + QS + 32 * il + 16 * h + 4 * t);
-                uint32_t wb = ld32(rb + QS + 32 * il + 16 * h + 4 * t);
-                uint32_t wa8 = wa >> 8, wb8 = wb >> 8;
-                uint32_t la0 = lop3_and_or(wa, 0x000F000Fu, H2_MAGIC), la1 = lop3_and_or(wa8, 0x000F000Fu, H2_MAGIC);
-                uint32_t lb0 = lop3_and_or(wb, 0x000F000Fu, H2_MAGIC), lb1 = lop3_and_or(wb8, 0x000F000Fu, H2_MAGIC);
-                uint32_t ha0 = lop3_and_or(wa, 0x00F000F0u, H2_MAGIC), ha1 = lop3_and_or(wa8, 0x00F000F0u, H2_MAGIC);
-                uint32_t hb0 = lop3_and_or(wb, 0x00F000F0u, H2_MAGIC), hb1 = lop3_and_or(wb8, 0x00F000F0u, H2_MAGIC);
+            for (int e = 0; e < 2; ++e) {
+                const uint32_t a = wa[i + e], b = wb[i + e], a8 = a >> 8, b8 = b >> 8;
+                uint32_t la0 = lop3_and_or(a, 0x000F000Fu, H2_MAGIC), la1 = lop3_and_or(a8, 0x000F000Fu, H2_MAGIC);
+                uint32_t lb0 = lop3_and_or(b, 0x000F000Fu, H2_MAGIC), lb1 = lop3_and_or(b8, 0x000F000Fu, H2_MAGIC);
+                uint32_t hA0 = lop3_and_or(a, 0x00F000F0u, H2_MAGIC), hA1 = lop3_and_or(a8, 0x00F000F0u, H2_MAGIC);
+                uint32_t hB0 = lop3_and_or(b, 0x00F000F0u, H2_MAGIC), hB1 = lop3_and_or(b8, 0x00F000F0u, H2_MAGIC);
                 if constexpr (Q5) {
-                    // 5th bit: qh[l] bit j0 (low nibbles) / j1 (high nibbles), dequant_q5_k.glsl:57-69
-                    const uint32_t qa = ld32(ra + 16 + 16 * h + 4 * t), qb = ld32(rb + 16 + 16 * h + 4 * t);
-                    auto lo02 = [&](uint32_t q) { return j0 <= 4 ? (q << (4 - j0)) : (q >> (j0 - 4)); };
-                    la0 = lop3_and_or(lo02(qa), 0x00100010u, la0);
-                    lb0 = lop3_and_or(lo02(qb), 0x00100010u, lb0);
-                    la1 = lop3_and_or(qa >> (4 + j0), 0x00100010u, la1);
-                    lb1 = lop3_and_or(qb >> (4 + j0), 0x00100010u, lb1);
-                    ha0 = lop3_and_or(qa << (8 - j1), 0x01000100u, ha0);
-                    hb0 = lop3_and_or(qb << (8 - j1), 0x01000100u, hb0);
-                    ha1 = lop3_and_or(qa >> j1, 0x01000100u, ha1);
-                    hb1 = lop3_and_or(qb >> j1, 0x01000100u, hb1);
+                    // qh byte l bit 2t -> code bit 4 (low), bit 2t+1 -> code bit 8 of the 16q form (high)
+                    const uint32_t qa = ha[i + e], qb = hb[i + e];
+                    const int s = 2 * t;
+                    la0 = lop3_and_or(s <= 4 ? qa << (4 - s) : qa >> (s - 4), 0x00100010u, la0);
+                    lb0 = lop3_and_or(s <= 4 ? qb << (4 - s) : qb >> (s - 4), 0x00100010u, lb0);
+                    la1 = lop3_and_or(qa >> (4 + s), 0x00100010u, la1);
+                    lb1 = lop3_and_or(qb >> (4 + s), 0x00100010u, lb1);
+                    hA0 = lop3_and_or(qa << (7 - s), 0x01000100u, hA0);
+                    hB0 = lop3_and_or(qb << (7 - s), 0x01000100u, hB0);
+                    hA1 = lop3_and_or(qa >> (s + 1), 0x01000100u, hA1);
+                    hB1 = lop3_and_or(qb >> (s + 1), 0x01000100u, hB1);
                 }
-                const uint32_t alo[4] = {hfma2_u(la0, sla, cla), hfma2_u(lb0, slb, clb), hfma2_u(la1, sla, cla),
-                                         hfma2_u(lb1, slb, clb)};
-                const uint32_t ahi[4] = {hfma2_u(ha0, sha, cha), hfma2_u(hb0, shb, chb), hfma2_u(ha1, sha, cha),
-                                         hfma2_u(hb1, shb, chb)};
-                uint32_t b0, b1, b2, b3;
-                xfrag(xc, 64 * il + 16 * h, t, b0, b1);
-                xfrag(xc, 64 * il + 32 + 16 * h, t, b2, b3);
-                mma_16816(p1[h], alo, b0, b1);
-                mma_16816(p1[h], ahi, b2, b3);
+                const uint32_t AL[4] = {hfma2_u(la0, ka.sl, ka.cl), hfma2_u(lb0, kb.sl, kb.cl), hfma2_u(la1, ka.sl, ka.cl),
+                                        hfma2_u(lb1, kb.sl, kb.cl)};
+                const uint32_t AH[4] = {hfma2_u(hA0, ka.sh, ka.ch), hfma2_u(hB0, kb.sh, kb.ch), hfma2_u(hA1, ka.sh, ka.ch),
+                                        hfma2_u(hB1, kb.sh, kb.ch)};
+                if (e == 0) {
+                    mma_16816(p0, AL, xl.x, xl.y);
+                    mma_16816(p0, AH, xh.x, xh.y);
+                } else {
+                    mma_16816(p1, AL, xl.z, xl.w);
+                    mma_16816(p1, AH, xh.z, xh.w);
+                }
             }
         }
-        float p2[4];
-        zero4(p2);
-        if constexpr (IL0 == 0) {
-            // thread t holds sub-blocks 2t, 2t+1: A = (m, m) for rows g, g+8; B = sums (hi | lo)
-            const uint32_t sel = (t & 1) ? 0x4342u : 0x4140u;
-            uint32_t am[4];
-            am[0] = am[2] = hsub2_u(prmt(t < 2 ? ka.mA : ka.mB, 0x64646464u, sel), H2_1024);
-            am[1] = am[3] = hsub2_u(prmt(t < 2 ? kb.mA : kb.mB, 0x64646464u, sel), H2_1024);
-            const uint2 v = *reinterpret_cast<const uint2 *>(xs + 8 * t);
-            mma_16816(p2, am, v.x, v.y);
-        }
-        const float dma = IL0 == 0 ? hbits(ra + 2) : 0.f, dmb = IL0 == 0 ? hbits(rb + 2) : 0.f;
+        const uint2 sv = *reinterpret_cast<const uint2 *>(xs + 8 * t);
+        float pm[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t am[4] = {ka.am, kb.am, ka.am, kb.am};
+        mma_16816(pm, am, sv.x, sv.y);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const float d = i < 2 ? da : db, dm = i < 2 ? dma : dmb;
-            acc[i] = fmaf(-dm, p2[i], fmaf(d, p1[0][i] + p1[1][i], acc[i]));
+            const float d = i < 2 ? ka.d : kb.d, dm = i < 2 ? ka.dm : kb.dm;
+            acc[i] = fmaf(-dm, pm[i], fmaf(d, p0[i] + p1[i], acc[i]));
         }
     }
 };
 
-template <> struct Step<VKF_DEQUANT_Q4_K> {
-    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
-                                               const uint8_t *xs, int t, int part, int, float (&acc)[4]) {
-        StepK<false, 0, 4>::run(ra, rb, xc, xs, t, acc);
+// M = 1 form of the K-quant decode.  With one activation column, seven of
+// the MMA's eight B columns would be idle; here they carry the sub-blocks.
+// Lane (g', t) supplies its activation fragment only in column g' = t (low
+// nibble MMAs) or g' = 4 + t (high nibble MMAs) and zero registers elsewhere
+// (a predicated-off load costs no shared-memory bandwidth), so
+// column t of every low MMA accumulates thread t's sub-block 2t and column
+// 4 + t of every high MMA sub-block 2t+1.  The A operand is the raw
+// "1024 + q" / "1024 + 16q" code (no fp16 scaling); after the super-block's
+// 16 MMAs each column holds  1024 * X_j + f_j * sum_l q_l x_l  exactly up to
+// fp32 accumulation (X_j the sub-block's activation sum, f_j = 1 or 16), and
+// thread (g, t), which owns columns 2t and 2t+1 (sub-blocks j1 = 4(t & 1) +
+// t / 2 and j1 + 2), applies
+//     acc += (d*sc_j/f_j) * D_j - (1024 * d*sc_j/f_j + dmin*m_j) * X_j.
+// The per-column sums are folded into one value per row at the end of the
+// row block (finish).
+__host__ __device__ __forceinline__ int m1_first_sub(int t) { return 4 * (t & 1) + (t >> 1); }
+// Position (t, e) of sub-block j in the per-super-block sums [t][e] (floats).
+__host__ __device__ __forceinline__ int m1_sum_slot(int j) {
+    const int e = (j >> 1) & 1, b = j - 2 * e;  // b in {0, 1, 4, 5}
+    const int t = 2 * (b & 1) + (b >> 2);
+    return 2 * t + e;
+}
+
+template <bool Q5> struct StepK1 {
+    static constexpr bool OWNED = true;
+    __device__ __forceinline__ static float byte_f(uint32_t w, uint32_t b) {
+        return __uint_as_float(prmt(w, 0x4B000000u, b | 0x7540u)) - 8388608.0f;  // [w.b, 0, 0, 0x4B]
+    }
+    // xu: the unit's activations; lo_on / hi_on: this lane feeds column t /
+    // 4 + t (the other lanes' fragments are zero registers, not loads).
+    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xu, bool lo_on,
+                                               bool hi_on, const float *xs, int t, float (&acc)[4]) {
+        constexpr int QS = Q5 ? 48 : 16;
+        const uint4 hA = lds128(ra), hB = lds128(rb);
+        uint32_t wa[8], wb[8];
+        {
+            const uint4 a0 = lds128(ra + QS + 32 * t), a1 = lds128(ra + QS + 16 + 32 * t);
+            const uint4 b0 = lds128(rb + QS + 32 * t), b1 = lds128(rb + QS + 16 + 32 * t);
+            wa[0] = a0.x; wa[1] = a0.y; wa[2] = a0.z; wa[3] = a0.w; wa[4] = a1.x; wa[5] = a1.y; wa[6] = a1.z; wa[7] = a1.w;
+            wb[0] = b0.x; wb[1] = b0.y; wb[2] = b0.z; wb[3] = b0.w; wb[4] = b1.x; wb[5] = b1.y; wb[6] = b1.z; wb[7] = b1.w;
+        }
+        uint32_t ha[8], hb[8];
+        if constexpr (Q5) {
+            const uint4 a0 = lds128(ra + 16), a1 = lds128(ra + 32), b0 = lds128(rb + 16), b1 = lds128(rb + 32);
+            ha[0] = a0.x; ha[1] = a0.y; ha[2] = a0.z; ha[3] = a0.w; ha[4] = a1.x; ha[5] = a1.y; ha[6] = a1.z; ha[7] = a1.w;
+            hb[0] = b0.x; hb[1] = b0.y; hb[2] = b0.z; hb[3] = b0.w; hb[4] = b1.x; hb[5] = b1.y; hb[6] = b1.z; hb[7] = b1.w;
+        }
+        float D0[4] = {0.f, 0.f, 0.f, 0.f}, D1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+            uint4 xl = make_uint4(0, 0, 0, 0), xh = make_uint4(0, 0, 0, 0);
+            if (lo_on) xl = lds128(xu + owned_group_offset(64 * t + 4 * i));
+            if (hi_on) xh = lds128(xu + owned_group_offset(64 * t + 32 + 4 * i));
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const uint32_t a = wa[i + e], b = wb[i + e], a8 = a >> 8, b8 = b >> 8;
+                uint32_t AL[4] = {lop3_and_or(a, 0x000F000Fu, H2_MAGIC), lop3_and_or(b, 0x000F000Fu, H2_MAGIC),
+                                  lop3_and_or(a8, 0x000F000Fu, H2_MAGIC), lop3_and_or(b8, 0x000F000Fu, H2_MAGIC)};
+                uint32_t AH[4] = {lop3_and_or(a, 0x00F000F0u, H2_MAGIC), lop3_and_or(b, 0x00F000F0u, H2_MAGIC),
+                                  lop3_and_or(a8, 0x00F000F0u, H2_MAGIC), lop3_and_or(b8, 0x00F000F0u, H2_MAGIC)};
+                if constexpr (Q5) {
+                    const uint32_t qa = ha[i + e], qb = hb[i + e];
+                    const int s = 2 * t;
+                    AL[0] = lop3_and_or(s <= 4 ? qa << (4 - s) : qa >> (s - 4), 0x00100010u, AL[0]);
+                    AL[1] = lop3_and_or(s <= 4 ? qb << (4 - s) : qb >> (s - 4), 0x00100010u, AL[1]);
+                    AL[2] = lop3_and_or(qa >> (4 + s), 0x00100010u, AL[2]);
+                    AL[3] = lop3_and_or(qb >> (4 + s), 0x00100010u, AL[3]);
+                    AH[0] = lop3_and_or(qa << (7 - s), 0x01000100u, AH[0]);
+                    AH[1] = lop3_and_or(qb << (7 - s), 0x01000100u, AH[1]);
+                    AH[2] = lop3_and_or(qa >> (s + 1), 0x01000100u, AH[2]);
+                    AH[3] = lop3_and_or(qb >> (s + 1), 0x01000100u, AH[3]);
+                }
+                float (&D)[4] = e ? D1 : D0;
+                mma_16816(D, AL, e ? xl.z : xl.x, e ? xl.w : xl.y);
+                mma_16816(D, AH, e ? xh.z : xh.x, e ? xh.w : xh.y);
+            }
+        }
+        // Scales of the thread's sub-blocks j1, j1 + 2 for both rows.
+        const uint32_t b1 = (uint32_t)(t >> 1), b2 = b1 + 2;
+        const bool hi_sb = t >= 2;  // columns 4..7: high-nibble sub-blocks (codes carry 16q)
+        const float2 xv = *reinterpret_cast<const float2 *>(xs + 2 * t);
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const uint4 h = r ? hB : hA;
+            uint32_t scw, mw;
+            if (t & 1) {  // sub-blocks 4..7
+                scw = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+                mw = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+            } else {
+                scw = h.y & 0x3F3F3F3Fu;
+                mw = h.z & 0x3F3F3F3Fu;
+            }
+            const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(&h.x));
+            const float df = hi_sb ? dd.x * 0.0625f : dd.x;
+            const float s1a = df * byte_f(scw, b1), s1b = df * byte_f(scw, b2);
+            const float c2a = fmaf(1024.0f, s1a, dd.y * byte_f(mw, b1));
+            const float c2b = fmaf(1024.0f, s1b, dd.y * byte_f(mw, b2));
+            float &o0 = acc[2 * r], &o1 = acc[2 * r + 1];
+            o0 = fmaf(-c2a, xv.x, fmaf(s1a, D0[2 * r] + D1[2 * r], o0));
+            o1 = fmaf(-c2b, xv.y, fmaf(s1b, D0[2 * r + 1] + D1[2 * r + 1], o1));
+        }
+    }
+    // Row block end: fold the 8 sub-block columns into column 0 (lanes t = 0).
+    __device__ __forceinline__ static void finish(float (&acc)[4]) {
+        float r0 = acc[0] + acc[1], r1 = acc[2] + acc[3];
+        r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
+        r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
+        r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
+        r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
+        acc[0] = r0;
+        acc[1] = 0.f;
+        acc[2] = r1;
+        acc[3] = 0.f;
     }
 };
-template <> struct Step<VKF_DEQUANT_Q5_K> {
-    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
-                                               const uint8_t *xs, int t, int part, int, float (&acc)[4]) {
-        StepK<true, 0, 4>::run(ra, rb, xc, xs, t, acc);
-    }
-};
+
+template <> struct Step<VKF_DEQUANT_Q4_K> : StepK<false> {};
+template <> struct Step<VKF_DEQUANT_Q5_K> : StepK<true> {};
 
 // Q6_K (dequant_q6_k.glsl:28-58): value = d * sc16 * (q6 - 32), one int8 scale
 // per 16 values; A operand = q6 - 32 (exact), each MMA's partial scaled by
@@ -301,8 +438,9 @@ template <int IP> struct StepQ6 {
 };
 
 template <> struct Step<VKF_DEQUANT_Q6_K> {
+    static constexpr bool OWNED = false;
     __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
-                                               const uint8_t *, int t, int part, int, float (&acc)[4]) {
+                                               const uint8_t *, int t, int, float (&acc)[4]) {
         StepQ6<0>::run(ra, rb, xc, t, acc);
         StepQ6<1>::run(ra, rb, xc, t, acc);
     }

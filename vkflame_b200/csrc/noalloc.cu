@@ -23,7 +23,7 @@ int gemv_launch_raw(int wtype, const void *W, const void *X, int64_t ldx_bytes, 
 namespace noalloc {
 
 // Partial sums: two 128-float slots per CTA, for up to NOALLOC_MAX_CTAS CTAs
-// (the GEMV runs at most two CTAs per SM).  Counters: one per 16-row block,
+// (the GEMV runs one CTA per SM).  Counters: one per 16-row block,
 // so N <= NOALLOC_MAX_ROWS.  512 KiB + 64 KiB + 4 bytes in total.
 constexpr int NOALLOC_MAX_CTAS = 512;
 constexpr int NOALLOC_MAX_ROWS = 262144;
