@@ -191,6 +191,10 @@ def cpu_baseline_gemv(qtype, N, K, M, budget_s=12.0):
 HIDDEN, FFN, VOCAB, LAYERS = 5120, 13824, 152064, 48
 HEADS, KV_HEADS, HEAD_DIM = 40, 8, 128
 METRIC = "aggregate weight-streaming GB/s, 48-layer Qwen2-14B Q4_K_M linear stack, M=1 decode"
+# DRAM bytes read / algorithmic weight bytes of one gemv_kernel launch, from
+# ncu captures of the Q4_K (K=5120, N=13824: 39.890 / 39.855 MB) and Q6_K
+# (K=13824, N=5120: 58.172 / 58.099 MB) shapes of the stack.
+GEMV_TRAFFIC_RATIO = 1.001
 
 
 def stack_groups():
@@ -309,7 +313,11 @@ def bench_stack(args, world, rank, local, dist):
                    "l2": "weights (9.0 GB) exceed L2; no flush needed"},
         "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks.get("hbm_gbs") else "fallback",
-                     "traffic": None, "note": "per-GPU weight bytes / device time per token (whole graph)"},
+                     "traffic": st.weight_bytes / launches_per_step * GEMV_TRAFFIC_RATIO,
+                     "note": "dominant kernel = gemv_kernel, every launch of the timed graph: algorithmic weight "
+                             "bytes per launch / average launch time (graph time / launches); traffic = DRAM "
+                             "bytes per launch, from the ncu captures of the same kernel on the stack's shapes "
+                             "(ratio to algorithmic bytes, profiles/gemv_*.md)"},
         "e2e": {"value": total_bytes / (ems * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": HIDDEN * 2,
                 "d2h_bytes_per_step": int(st.out.numel()) * 2, "ms_per_step": ems},
         "gpu_launches": launches_per_step * args.steps, "clocks": clocks,
