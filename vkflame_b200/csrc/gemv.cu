@@ -34,10 +34,21 @@
 #include "gemv_q.cuh"
 
 #include <algorithm>
+#include <type_traits>
 #include <cstdlib>
 
 namespace vkf {
 namespace gemv {
+
+#ifdef VKF_GEMV_TIMING
+// Debug builds only: per-warp cycle counters [cta][warp][phase].
+__device__ unsigned long long g_timing[512][32][8];
+#define VKF_T0() const long long _t0 = clock64()
+#define VKF_TACC(ph, t0) atomicAdd(&g_timing[blockIdx.x][threadIdx.x >> 5][ph], (unsigned long long)(clock64() - (t0)))
+#else
+#define VKF_T0()
+#define VKF_TACC(ph, t0)
+#endif
 
 constexpr int NST_MAX = 8;            // ring depth cap
 constexpr int ROW_BUDGET = 4400;      // max bytes of one row per item
@@ -62,13 +73,14 @@ struct Args {
     int stage_bytes;
     int xpr;           // smem pitch of one resident activation column
     int xsp;           // smem pitch of one column's sub-block sums
-    int slots;         // partial slots (row blocks in flight)
+    int slots;         // parked-partial slots (row blocks in flight)
     int off_sums, off_ring, off_red, off_bar;
     float *ws;         // partials of cut row blocks: [G][2][16 * M]
     int *cnt;          // per-row-block arrival counters (zero between launches)
     unsigned *err;
     int y_f16;
     int prefetch;      // stream weights before the previous kernel on the stream completes
+    int whole_tiles;   // S == 1 and W 16-byte aligned: one copy per row block
 };
 
 __device__ __forceinline__ int first_item(int c, const Args &a) { return (int)((int64_t)c * a.I / a.G); }
@@ -91,7 +103,9 @@ __device__ __forceinline__ void store_y(const Args &a, int m, int n, float v) {
 // their fp32 sum: split into hi + lo fp16 in the min-term MMA's B layout
 // [super-block][t] = (hi 2t, hi 2t+1, lo 2t, lo 2t+1), or (M = 1 column
 // form) as fp32 in the [super-block][t][2] order of the thread's sub-blocks.
-template <bool OWN, bool KQ, bool COLS, int NTC>
+// SUMS: 0 none; 1 K-quant hi + lo fp16 (min-term MMA); 2 K-quant fp32 in
+// the column form's [t][2] order; 3 fp32 per 16-value group (Q6_K column form).
+template <bool OWN, int SUMS, int NTC>
 __device__ __forceinline__ void load_activations(const Args &a, uint8_t *xs, uint8_t *sums) {
     const int nsb = a.K / 32, jobs = a.M * nsb;
     for (int j = threadIdx.x; j < jobs; j += NTC) {
@@ -114,7 +128,7 @@ __device__ __forceinline__ void load_activations(const Args &a, uint8_t *xs, uin
                 *reinterpret_cast<uint2 *>(col + off) = p;
             }
         }
-        if constexpr (KQ) {
+        if constexpr (SUMS != 0) {
             float part[4];
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
@@ -127,8 +141,14 @@ __device__ __forceinline__ void load_activations(const Args &a, uint8_t *xs, uin
                 }
                 part[c] = s2;
             }
+            if constexpr (SUMS == 3) {
+                float *o = reinterpret_cast<float *>(sums + m * a.xsp + (sb / 8) * 64) + 2 * (sb % 8);
+                o[0] = part[0] + part[1];
+                o[1] = part[2] + part[3];
+                continue;
+            }
             const float sum = (part[0] + part[1]) + (part[2] + part[3]);
-            if constexpr (COLS) {
+            if constexpr (SUMS == 2) {
                 reinterpret_cast<float *>(sums + m * a.xsp + (sb / 8) * 32)[m1_sum_slot(sb % 8)] = sum;
                 continue;
             }
@@ -141,22 +161,29 @@ __device__ __forceinline__ void load_activations(const Args &a, uint8_t *xs, uin
     }
 }
 
+// Slot arithmetic shared by consumers and the reducer: row block number k of
+// this CTA (k = 0, 1, ...) uses slot k % slots, phase (k / slots) & 1.
 template <int QT, int CW, bool M1>
-__global__ void __launch_bounds__(32 * (CW + 1), 1) gemv_kernel(const __grid_constant__ Args a) {
+__global__ void __launch_bounds__(32 * (CW + 2), 1) gemv_kernel(const __grid_constant__ Args a) {
     constexpr int NTC = 32 * CW;
     constexpr int QK = Fmt<QT>::QK, BB = Fmt<QT>::BB;
     constexpr int UB = (256 / QK) * BB;  // bytes of one 256-value unit of a row
     constexpr bool KQ = QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K;
     constexpr bool OWN = Step<QT>::OWNED;
-    constexpr bool COLS = M1 && KQ;  // sub-block-column decode (StepK1)
+    constexpr bool Q6 = QT == VKF_DEQUANT_Q6_K;
+    constexpr bool COLS = M1 && (KQ || Q6);  // column-form decode (StepK1, StepQ6c)
+    constexpr int SUMS = COLS ? (KQ ? 2 : 3) : (KQ ? 1 : 0);
+    constexpr int PW = COLS ? 2 : 4;         // parked floats per lane
+    constexpr int PRODUCER = CW, REDUCER = CW + 1;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *xs = smem;
     uint8_t *sums = smem + a.off_sums;
     uint8_t *ring = smem + a.off_ring;
-    float *red = reinterpret_cast<float *>(smem + a.off_red);
+    float *park = reinterpret_cast<float *>(smem + a.off_red);  // [slot][warp][lane][PW]
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + a.off_bar);
     uint64_t *empty = full + NST_MAX;
-    int *slotcnt = reinterpret_cast<int *>(empty + NST_MAX);  // arrivals per reduction slot
+    uint64_t *parked = empty + NST_MAX;   // per slot: CW consumer arrivals
+    uint64_t *freed = parked + MAX_SLOTS; // per slot: reducer done
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cta = blockIdx.x;
@@ -170,12 +197,15 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1) gemv_kernel(const __grid_con
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], CW);
         }
+        for (int s = 0; s < a.slots; ++s) {
+            mbar_init(&parked[s], CW);
+            mbar_init(&freed[s], 1);
+        }
         fence_mbar_init();
     }
-    if (threadIdx.x < MAX_SLOTS) slotcnt[threadIdx.x] = 0;
     __syncthreads();
 
-    if (warp == CW) {
+    if (warp == PRODUCER) {
         // ---------------- producer ----------------
         // Weights that no kernel writes (a.prefetch) are streamed at once;
         // otherwise the producer too waits for the previous kernel.
@@ -189,23 +219,36 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1) gemv_kernel(const __grid_con
             // 32-value-block format holds only the blocks that exist), widened
             // to whole 16-byte granules: a 16-byte aligned granule never
             // crosses a page, so the few bytes read either side are mapped.
-            const int64_t b0 = (int64_t)u0 * UB;
-            const int64_t b1 = min((int64_t)(u0 + nu) * UB, a.row_bytes);
-            const int row = tile * 16 + lane;
-            uint32_t sz = 0;
-            const uint8_t *src = nullptr;
-            if (lane < 16 && row < a.N) {
-                const uint8_t *p = a.W + (int64_t)row * a.row_bytes + b0;
-                const uint32_t off = (uint32_t)((uintptr_t)p & 15);
-                src = p - off;
-                sz = (uint32_t)((off + (b1 - b0) + 15) & ~15);
-            }
-            uint32_t total = sz;
+            if (a.whole_tiles) {
+                // Whole rows: the row block is one contiguous, 16-byte aligned
+                // range of the matrix and lands as one copy (one TMA operation
+                // per row block instead of one per row: the per-row form is
+                // held to ~4.8 TB/s by the operation rate at 1.4 KB rows).
+                if (lane == 0) {
+                    const int rows = min(16, a.N - tile * 16);
+                    const uint32_t sz = (uint32_t)(((int64_t)rows * a.row_bytes + 15) & ~(int64_t)15);
+                    mbar_arrive_expect_tx(&full[s], sz);
+                    bulk_g2s(ring + s * a.stage_bytes, a.W + (int64_t)tile * 16 * a.row_bytes, sz, &full[s]);
+                }
+            } else {
+                const int64_t b0 = (int64_t)u0 * UB;
+                const int64_t b1 = min((int64_t)(u0 + nu) * UB, a.row_bytes);
+                const int row = tile * 16 + lane;
+                uint32_t sz = 0;
+                const uint8_t *src = nullptr;
+                if (lane < 16 && row < a.N) {
+                    const uint8_t *p = a.W + (int64_t)row * a.row_bytes + b0;
+                    const uint32_t off = (uint32_t)((uintptr_t)p & 15);
+                    src = p - off;
+                    sz = (uint32_t)((off + (b1 - b0) + 15) & ~15);
+                }
+                uint32_t total = sz;
 #pragma unroll
-            for (int o = 8; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], total);
-            __syncwarp();
-            if (sz) bulk_g2s(ring + s * a.stage_bytes + lane * a.rpb, src, sz, &full[s]);
+                for (int o = 8; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+                if (lane == 0) mbar_arrive_expect_tx(&full[s], total);
+                __syncwarp();
+                if (sz) bulk_g2s(ring + s * a.stage_bytes + lane * a.rpb, src, sz, &full[s]);
+            }
             if (++step == a.S) {
                 step = 0;
                 ++tile;
@@ -218,10 +261,114 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1) gemv_kernel(const __grid_con
         return;
     }
 
+    const int rows16m = 16 * a.M;
+    if (warp == REDUCER) {
+        // ---------------- reducer ----------------
+        // Walks the CTA's row blocks in order: waits until all consumer warps
+        // have parked their partials, sums them in warp order (deterministic),
+        // stores Y, and frees the slot.  A row block cut between CTAs is
+        // published to scratch; its last contributor sums all partials in CTA
+        // order.  None of this is on the consumers' path.
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        const int first_tile = it0 / a.S, last_tile = (it1 - 1) / a.S;
+        bool ok = true;
+        for (int tb = first_tile, k = 0; tb <= last_tile && it1 > it0; ++tb, ++k) {
+            const int sl = k % a.slots;
+            if (ok) ok = mbar_wait(&parked[sl], (uint32_t)(k / a.slots) & 1u, a.err);
+            const float *q = park + (size_t)sl * CW * 32 * PW;
+            float o[4];
+            if constexpr (COLS) {
+                // lane = (row r = lane & 15, warp half h = lane >> 4): rows g < 8
+                // are .x of lanes g*4 + t, rows g + 8 are .y.
+                const int r = lane & 15, h = lane >> 4, g = r & 7, comp = r >> 3;
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < CW / 2; ++w)
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) v += q[((h * (CW / 2) + w) * 32 + g * 4 + t) * 2 + comp];
+                v += __shfl_xor_sync(0xffffffffu, v, 16);
+                o[0] = v;
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int rc = lane + 32 * j;
+                    o[j] = 0.f;
+                    if (rc < rows16m) {
+                        const int r = rc / a.M, c = rc - r * a.M;
+                        const int g = r & 7, comp = (r >> 3) * 2 + (c & 1), l = g * 4 + (c >> 1);
+#pragma unroll 4
+                        for (int w = 0; w < CW; ++w) o[j] += q[(w * 32 + l) * 4 + comp];
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&freed[sl]);
+            const bool whole = tb * a.S >= it0 && (tb + 1) * a.S <= it1;
+            if (whole) {
+                if constexpr (COLS) {
+                    if (lane < 16 && tb * 16 + lane < a.N) store_y(a, 0, tb * 16 + lane, o[0]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int rc = lane + 32 * j, r = rc / a.M, c = rc - r * a.M;
+                        if (rc < rows16m && tb * 16 + r < a.N) store_y(a, c, tb * 16 + r, o[j]);
+                    }
+                }
+                continue;
+            }
+            // A row block cut between CTAs: publish this CTA's partial; the last
+            // contributor to arrive sums all partials in CTA order and stores Y.
+            const int which = tb == first_tile ? 0 : 1;
+            float *wsp = a.ws + ((int64_t)cta * 2 + which) * rows16m;
+            if constexpr (COLS) {
+                if (lane < 16) wsp[lane] = o[0];
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (lane + 32 * j < rows16m) wsp[lane + 32 * j] = o[j];
+            }
+            const int c_first = cta_of_item(tb * a.S, a), c_last = cta_of_item((tb + 1) * a.S - 1, a);
+            __syncwarp();
+            int fin = 0;
+            if (lane == 0) {
+                __threadfence();
+                fin = atomicAdd(&a.cnt[tb], 1) == c_last - c_first;
+                if (fin) __threadfence();
+            }
+            if (!__shfl_sync(0xffffffffu, fin, 0)) continue;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int rc = lane + 32 * j;
+                if (rc >= rows16m) continue;
+                float v = 0.f;
+                for (int c = c_first; c <= c_last; ++c) {
+                    const int wc = tb == first_item(c, a) / a.S ? 0 : 1;
+                    v += __ldcg(a.ws + ((int64_t)c * 2 + wc) * rows16m + rc);
+                }
+                const int r = rc / a.M, col = rc - r * a.M;
+                if (tb * 16 + r < a.N) store_y(a, col, tb * 16 + r, v);
+            }
+            if (lane == 0) a.cnt[tb] = 0;
+        }
+        return;
+    }
+
     // ---------------- consumers ----------------
+#ifdef VKF_GEMV_TIMING
+    const long long tp0 = clock64();
+#endif
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    load_activations<OWN, KQ, COLS, NTC>(a, xs, sums);
+    load_activations<OWN, SUMS, NTC>(a, xs, sums);
     consumer_bar<CW>();
+#ifdef VKF_GEMV_TIMING
+    if (lane == 0) VKF_TACC(2, tp0);
+    const long long tl0 = clock64();
+    struct TEnd {
+        long long t;
+        int lane;
+        __device__ ~TEnd() { if (lane == 0) VKF_TACC(3, t); }
+    } tend{tl0, lane};
+#endif
 
     const int g = lane >> 2, t = lane & 3;
     // Lanes of columns >= M read a real column (their outputs are dropped),
@@ -229,43 +376,79 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1) gemv_kernel(const __grid_con
     const int xcol = g % a.M;
     const uint8_t *xg = xs + xcol * a.xpr;
     const uint8_t *sg = sums + xcol * a.xsp;
-    const int rows16m = 16 * a.M;
     // After a bounded wait gives up (error bit already set) the warp keeps
-    // walking the same items without waiting or computing, so every consumer
-    // warp still reaches the same barriers.
+    // walking the same items without waiting or computing, so every warp
+    // still makes the same barrier arrivals.
     bool ok = true;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     int tile = it0 / a.S, step = it0 - tile * a.S, s = 0;
     uint32_t ph = 0;
     int ubase = 0;  // units of this CTA's earlier items, mod CW
-    int slot = 0, done_tile = tile;
-    const int first_tile = tile;
+    int k = 0;      // row blocks finished by this CTA
     for (int it = it0; it < it1; ++it) {
+#ifdef VKF_GEMV_TIMING
+        const long long tw0 = clock64();
+#endif
         if (ok) ok = mbar_wait(&full[s], ph, a.err);
+#ifdef VKF_GEMV_TIMING
+        if (lane == 0) VKF_TACC(0, tw0);
+        const long long td0 = clock64();
+#endif
         const int u0 = step * a.upi, nu = min(a.upi, a.units - u0);
         if (ok) {
             const uint8_t *st = ring + s * a.stage_bytes;
-            const int64_t row_a = (int64_t)tile * 16 + g;
-            const uintptr_t ga = (uintptr_t)a.W + row_a * a.row_bytes + (int64_t)u0 * UB;
-            const uintptr_t gb = ga + 8 * a.row_bytes;
-            const uint8_t *ra = st + g * a.rpb + (ga & 15), *rb = st + (g + 8) * a.rpb + (gb & 15);
+            const uint8_t *ra, *rb;
+            if (a.whole_tiles) {  // contiguous image of the row block
+                ra = st + g * a.row_bytes;
+                rb = ra + 8 * a.row_bytes;
+            } else {
+                const int64_t row_a = (int64_t)tile * 16 + g;
+                const uintptr_t ga = (uintptr_t)a.W + row_a * a.row_bytes + (int64_t)u0 * UB;
+                const uintptr_t gb = ga + 8 * a.row_bytes;
+                ra = st + g * a.rpb + (ga & 15);
+                rb = st + (g + 8) * a.rpb + (gb & 15);
+            }
             int u = warp - ubase;
             if (u < 0) u += CW;
-            for (; u < nu; u += CW) {
-                const int unit = u0 + u;
-                if constexpr (COLS) {
-                    StepK1<QT == VKF_DEQUANT_Q5_K>::run(ra + u * UB, rb + u * UB, xs + unit * 512, g == t, g == t + 4,
+            auto unit_step = [&](int uu) {
+                const int unit = u0 + uu;
+                if constexpr (COLS && KQ) {
+                    StepK1<QT == VKF_DEQUANT_Q5_K>::run(ra + uu * UB, rb + uu * UB, xs + unit * 512, g == t, g == t + 4,
                                                         reinterpret_cast<const float *>(sums + unit * 32), t, acc);
                 } else {
                     const int nblk = QK == 32 ? min(8, (a.K - unit * 256) / 32) : 8;
-                    Step<QT>::run(ra + u * UB, rb + u * UB, xg + unit * 512, sg + unit * 32, t, nblk, acc);
+                    Step<QT>::run(ra + uu * UB, rb + uu * UB, xg + unit * 512, sg + unit * 32, t, nblk, acc);
                 }
+            };
+            if constexpr (COLS && Q6) {
+                // Q6_K super-blocks are 210 bytes: a unit's words are 4-byte
+                // aligned or 2 mod 4 by its parity, uniformly across the warp
+                // when rows are a multiple of 4 bytes (K a multiple of 512).
+                for (; u < nu; u += CW) {
+                    const int unit = u0 + u;
+                    const uint8_t *pa = ra + u * UB, *pb = rb + u * UB;
+                    const float *x16 = reinterpret_cast<const float *>(sums + unit * 64);
+                    if ((((uintptr_t)pa | (uintptr_t)pb) & 3) == 0) StepQ6c::run<true>(pa, pb, xs + unit * 512, g, x16, t, acc);
+                    else StepQ6c::run<false>(pa, pb, xs + unit * 512, g, x16, t, acc);
+                }
+            } else {
+                for (; u < nu; u += CW) unit_step(u);
             }
         }
+#ifdef VKF_GEMV_TIMING
+        __syncwarp();
+        if (lane == 0) VKF_TACC(1, td0);
+#endif
+#ifdef VKF_GEMV_TIMING
+        const long long ta0 = clock64();
+#endif
         ubase += nu;
         while (ubase >= CW) ubase -= CW;
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+#ifdef VKF_GEMV_TIMING
+        if (lane == 0) VKF_TACC(5, ta0);
+#endif
         if (++s == a.nst) {
             s = 0;
             ph ^= 1u;
@@ -277,89 +460,51 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1) gemv_kernel(const __grid_con
         }
         if (!tile_end) continue;
 
-        if constexpr (COLS) StepK1<QT == VKF_DEQUANT_Q5_K>::finish(acc);
-        // Park this warp's partial of the finished row block in the block's
-        // slot; the last warp to arrive reduces the slot in warp order
-        // (deterministic) while the others go on decoding.  A warp runs at
-        // most nst items ahead of the slowest, so nst + 2 slots never alias.
-        float *p = red + (slot * CW + warp) * rows16m;
-        {
-            const int c0 = 2 * t, c1 = 2 * t + 1;
-            if (c0 < a.M) {
-                p[g * a.M + c0] = acc[0];
-                p[(g + 8) * a.M + c0] = acc[2];
-            }
-            if (c1 < a.M) {
-                p[g * a.M + c1] = acc[1];
-                p[(g + 8) * a.M + c1] = acc[3];
-            }
-            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+        // Park this warp's partial of the finished row block (one vector store
+        // per lane) and signal the reducer; a slot is reused only after the
+        // reducer has freed it (slots row blocks earlier).
+        const int sl = k % a.slots;
+#ifdef VKF_GEMV_TIMING
+        const long long tf0 = clock64();
+#endif
+        if (k >= a.slots && ok) ok = mbar_wait(&freed[sl], (uint32_t)(k / a.slots - 1) & 1u, a.err);
+#ifdef VKF_GEMV_TIMING
+        if (lane == 0) VKF_TACC(4, tf0);
+#endif
+        float *p = park + ((size_t)(sl * CW + warp) * 32 + lane) * PW;
+        if constexpr (COLS) {
+            *reinterpret_cast<float2 *>(p) = make_float2(acc[0] + acc[1], acc[2] + acc[3]);
+        } else {
+            *reinterpret_cast<float4 *>(p) = make_float4(acc[0], acc[1], acc[2], acc[3]);
         }
-        const int tb = done_tile, sl = slot;
-        ++done_tile;
-        if (++slot == a.slots) slot = 0;
+        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
         __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-            __threadfence_block();
-            last = atomicAdd(&slotcnt[sl], 1) == CW - 1;
-            if (last) __threadfence_block();
-        }
-        if (!__shfl_sync(0xffffffffu, last, 0)) continue;
-
-        const float *q = red + sl * CW * rows16m;
-        const bool whole = tb * a.S >= it0 && (tb + 1) * a.S <= it1;
-        float o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int rc = lane + 32 * j;
-            o[j] = 0.f;
-            if (rc < rows16m) {
-#pragma unroll 4
-                for (int w = 0; w < CW; ++w) o[j] += q[w * rows16m + rc];
-            }
-        }
-        __syncwarp();
-        if (lane == 0) slotcnt[sl] = 0;
-        if (whole) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int rc = lane + 32 * j, r = rc / a.M, c = rc - r * a.M;
-                if (rc < rows16m && tb * 16 + r < a.N) store_y(a, c, tb * 16 + r, o[j]);
-            }
-            continue;
-        }
-        // A row block cut between CTAs: publish this CTA's partial; the last
-        // contributor to arrive sums all partials in CTA order and stores Y.
-        const int which = tb == first_tile ? 0 : 1;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int rc = lane + 32 * j;
-            if (rc < rows16m) a.ws[((int64_t)cta * 2 + which) * rows16m + rc] = o[j];
-        }
-        const int c_first = cta_of_item(tb * a.S, a), c_last = cta_of_item((tb + 1) * a.S - 1, a);
-        __syncwarp();
-        int fin = 0;
-        if (lane == 0) {
-            __threadfence();
-            fin = atomicAdd(&a.cnt[tb], 1) == c_last - c_first;
-            if (fin) __threadfence();
-        }
-        if (!__shfl_sync(0xffffffffu, fin, 0)) continue;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int rc = lane + 32 * j;
-            if (rc >= rows16m) continue;
-            float v = 0.f;
-            for (int c = c_first; c <= c_last; ++c) {
-                const int wc = tb == first_item(c, a) / a.S ? 0 : 1;
-                v += __ldcg(a.ws + ((int64_t)c * 2 + wc) * rows16m + rc);
-            }
-            const int r = rc / a.M, col = rc - r * a.M;
-            if (tb * 16 + r < a.N) store_y(a, col, tb * 16 + r, v);
-        }
-        if (lane == 0) a.cnt[tb] = 0;
+        if (lane == 0) mbar_arrive(&parked[sl]);
+        ++k;
     }
+}
+
+// Worst shared-memory bank multiplicity of the decode's weight loads when rows
+// sit at `pitch` bytes: 16-byte loads of lanes (g, t) at g * pitch + 32 t in
+// 8-lane phases (owned mapping), or 4-byte loads at g * pitch + 4 t across
+// the warp (plain mapping).  A contiguous row block (one copy) is used only
+// where this stays <= 2.
+static int pitch_conflicts(int64_t pitch, bool owned) {
+    int worst = 0;
+    if (owned) {
+        if (pitch % 16) return 32;
+        for (int ph = 0; ph < 4; ++ph) {
+            int hits[8] = {};
+            for (int gg = 2 * ph; gg < 2 * ph + 2; ++gg)
+                for (int t = 0; t < 4; ++t) worst = std::max(worst, ++hits[(gg * (pitch / 16) + 2 * t) % 8]);
+        }
+    } else {
+        if (pitch % 4) return 32;
+        int hits[32] = {};
+        for (int gg = 0; gg < 8; ++gg)
+            for (int t = 0; t < 4; ++t) worst = std::max(worst, ++hits[(gg * (pitch / 4) + t) % 32]);
+    }
+    return worst;
 }
 
 template <int QT, int CW, bool M1>
@@ -368,7 +513,7 @@ struct Launcher {
     static constexpr int UB = (256 / QK) * BB;
     static constexpr bool KQ = QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K;
     static constexpr bool OWN = Step<QT>::OWNED;
-    static constexpr int NT = 32 * (CW + 1);
+    static constexpr int NT = 32 * (CW + 2);
 
     static int launch(Args &a, int sms, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap) {
         auto up = [](int64_t v, int64_t m) { return (v + m - 1) / m * m; };
@@ -377,13 +522,15 @@ struct Launcher {
         // columns 64 bytes apart mod 128 banks-wise, the plain layout's
         // 8-byte loads 32 bytes.
         a.xpr = (int)up((int64_t)a.units * 512, 128) + (OWN ? 64 : 32);
-        a.xsp = KQ ? (int)up((int64_t)a.units * 32, 16) : 0;
+        constexpr bool Q6 = QT == VKF_DEQUANT_Q6_K;
+        a.xsp = (M1 && Q6) ? a.units * 64 : KQ ? (int)up((int64_t)a.units * 32, 16) : 0;
         a.off_sums = a.M * a.xpr;
         const int x_end = (int)up(a.off_sums + (int64_t)a.M * a.xsp, 128);
         if (x_end > X_BUDGET) return VKF_ERR_UNSUPPORTED;
         const int rows16m = 16 * a.M;
-        const int slot_bytes = CW * rows16m * 4;
-        const int bar_bytes = 2 * NST_MAX * 8 + MAX_SLOTS * 4;
+        constexpr bool COLS = M1 && (KQ || QT == VKF_DEQUANT_Q6_K);
+        const int slot_bytes = CW * 32 * (COLS ? 2 : 4) * 4;
+        const int bar_bytes = 2 * NST_MAX * 8 + 2 * MAX_SLOTS * 8;
         const int avail = SMEM_MAX - x_end - bar_bytes - 128;
         a.T = (a.N + 15) / 16;
 
@@ -400,6 +547,8 @@ struct Launcher {
             const int ng = ((a.upi * UB + 15) / 16 + 1) | 1;  // odd granule count: rows 16 banks apart
             a.rpb = ng * 16;
             a.stage_bytes = 16 * a.rpb;
+            a.whole_tiles = a.S == 1 && ((uintptr_t)a.W & 15) == 0 && pitch_conflicts(a.row_bytes, OWN) <= 2;
+            if (a.whole_tiles) a.stage_bytes = (int)up(16 * a.row_bytes, 128);
             a.nst = std::min(NST_MAX, (avail - 2 * slot_bytes) / (a.stage_bytes + slot_bytes));
             if (a.nst >= 2 || a.upi == 1) break;
             a.upi = std::max(1, a.upi / 2);
@@ -447,8 +596,8 @@ constexpr int CW_DEFAULT = 8;
 
 template <int QT>
 static int launch_q(Args &a, int sms, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap) {
-    constexpr bool KQ = QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K;
-    if (KQ && a.M == 1) return Launcher<QT, CW_DEFAULT, true>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    constexpr bool COLS_FMT = QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K || QT == VKF_DEQUANT_Q6_K;
+    if (COLS_FMT && a.M == 1) return Launcher<QT, CW_DEFAULT, true>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
     return Launcher<QT, CW_DEFAULT, false>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
 }
 
@@ -465,6 +614,16 @@ static int dispatch(int wtype, Args &a, int sms, cudaStream_t stream, float *ws,
 }
 
 }  // namespace gemv
+
+#ifdef VKF_GEMV_TIMING
+extern "C" int vkf_gemv_timing(void *host, int reset) {
+    if (reset) {
+        static unsigned long long z[512 * 32 * 8];
+        return (int)cudaMemcpyToSymbol(gemv::g_timing, z, sizeof(z));
+    }
+    return (int)cudaMemcpyFromSymbol(host, gemv::g_timing, sizeof(gemv::g_timing));
+}
+#endif
 
 // Batch columns per launch so the resident activations fit the budget.
 int gemv_cols_per_launch(int K) {

@@ -437,6 +437,83 @@ template <int IP> struct StepQ6 {
     }
 };
 
+// Q6_K, M = 1 column form (see StepK1): the MMA of (ip, s, h) covers the 16
+// values of scale group 8 ip + 2 s + h (plain mapping: thread t holds
+// l = 16 h + 4 t .. + 3), and only lanes of column c = 2 s + h supply
+// activations, so after the 8 MMAs of half ip column c holds group
+// 8 ip + c:  D = 1024 X16 + f sum q x  with A the raw code "1024 + q" (s < 2,
+// f = 1) or "1024 + 16 q" (s >= 2, f = 16).  Thread (g, t) owns columns 2t and
+// 2t+1 (s = t, h = 0 / 1) and adds  d*sc * (D / f - (1024 / f + 32) * X16)
+// (the value is d*sc*(q - 32), dequant_q6_k.glsl:34-58).  The 6-bit codes are
+// built from one ql and one qh word per MMA with shifts shared by the four s:
+// qh << 4 places bits 0-1 at 4-5 (s = 0) and bits 4-5 at 8-9 (s = 2), qh << 2
+// serves s = 1 and s = 3, and >> 4 / >> 6 the same for bytes 1 and 3.
+// Super-blocks are 210 bytes: words of odd ones start 2 mod 4 and are read as
+// two aligned words and a byte permute (AL4 = false).
+struct StepQ6c {
+    static constexpr bool OWNED = false;
+    template <bool AL4> __device__ __forceinline__ static uint32_t w32(const uint8_t *p) {
+        if constexpr (AL4) return *reinterpret_cast<const uint32_t *>(p);
+        const uint32_t lo = *reinterpret_cast<const uint32_t *>(p - 2), hi = *reinterpret_cast<const uint32_t *>(p + 2);
+        return prmt(lo, hi, 0x5432);
+    }
+    // Codes of value pair (bytes 0,2) [pair 0] or (1,3) [pair 1] for s.
+    template <int S>
+    __device__ __forceinline__ static uint32_t code(uint32_t ql, uint32_t ql8, uint32_t h4, uint32_t h2, uint32_t hr4,
+                                                    uint32_t hr6, int pair) {
+        constexpr uint32_t NM = S < 2 ? 0x000F000Fu : 0x00F000F0u, HM = S < 2 ? 0x00300030u : 0x03000300u;
+        const uint32_t q = pair ? ql8 : ql;
+        const uint32_t hh = pair ? ((S & 1) ? hr6 : hr4) : ((S & 1) ? h2 : h4);
+        return lop3_and_or(q, NM, lop3_and_or(hh, HM, H2_MAGIC));
+    }
+    template <bool AL4>
+    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xu, int g,
+                                               const float *x16, int t, float (&acc)[4]) {
+        const float da = half_bits_to_float(ld_u16(ra + 208)), db = half_bits_to_float(ld_u16(rb + 208));
+        const float f = t >= 2 ? 0.0625f : 1.0f, c32 = t >= 2 ? 96.0f : 1056.0f;
+#pragma unroll
+        for (int ip = 0; ip < 2; ++ip) {
+            float D[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int o = 64 * ip + 16 * h + 4 * t, oh = 128 + 32 * ip + 16 * h + 4 * t;
+                const uint32_t a0 = w32<AL4>(ra + o), a1 = w32<AL4>(ra + o + 32), ah = w32<AL4>(ra + oh);
+                const uint32_t b0 = w32<AL4>(rb + o), b1 = w32<AL4>(rb + o + 32), bh = w32<AL4>(rb + oh);
+                const uint32_t a08 = a0 >> 8, a18 = a1 >> 8, b08 = b0 >> 8, b18 = b1 >> 8;
+                const uint32_t ah4 = ah << 4, ah2 = ah << 2, ahr4 = ah >> 4, ahr6 = ah >> 6;
+                const uint32_t bh4 = bh << 4, bh2 = bh << 2, bhr4 = bh >> 4, bhr6 = bh >> 6;
+#define VKF_Q6C_MMA(S, QA, QA8, QB, QB8)                                                                        \
+    {                                                                                                           \
+        const uint32_t A[4] = {code<S>(QA, QA8, ah4, ah2, ahr4, ahr6, 0), code<S>(QB, QB8, bh4, bh2, bhr4, bhr6, 0), \
+                               code<S>(QA, QA8, ah4, ah2, ahr4, ahr6, 1), code<S>(QB, QB8, bh4, bh2, bhr4, bhr6, 1)}; \
+        uint2 xv = make_uint2(0, 0);                                                                            \
+        if (g == 2 * S + h) xv = *reinterpret_cast<const uint2 *>(xu + (128 * ip + 32 * S + 16 * h + 4 * t) * 2); \
+        mma_16816(D, A, xv.x, xv.y);                                                                            \
+    }
+                VKF_Q6C_MMA(0, a0, a08, b0, b08)
+                VKF_Q6C_MMA(1, a1, a18, b1, b18)
+                VKF_Q6C_MMA(2, a0, a08, b0, b08)
+                VKF_Q6C_MMA(3, a1, a18, b1, b18)
+#undef VKF_Q6C_MMA
+            }
+            // Columns 2t, 2t+1 = groups 8 ip + 2t + h: int8 scales at 192 + 8 ip + 2t (+1).
+            const uint32_t sa = ld_u16(ra + 192 + 8 * ip + 2 * t), sb = ld_u16(rb + 192 + 8 * ip + 2 * t);
+            const float2 xg = *reinterpret_cast<const float2 *>(x16 + 8 * ip + 2 * t);
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const uint32_t sw = r ? sb : sa;
+                const float d = r ? db : da;
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    const float dsc = d * (float)(int8_t)(sw >> (8 * hh));
+                    float &o = acc[2 * r + hh];
+                    o = fmaf(dsc * f, D[2 * r + hh], fmaf(-dsc * c32, hh ? xg.y : xg.x, o));
+                }
+            }
+        }
+    }
+};
+
 template <> struct Step<VKF_DEQUANT_Q6_K> {
     static constexpr bool OWNED = false;
     __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xc,
