@@ -212,7 +212,7 @@ class Stack:
 
     def __init__(self, world, rank, dist, stream):
         import torch
-        from vkflame_b200 import rt
+        from vkflame_b200 import rt, shard
         self.rt, self.world, self.rank, self.dist, self.stream = rt, world, rank, dist, stream
         self.linears = []  # (qtype, K, Nshard, weight, input tensor, output shard, gathered output)
         self.x_h = torch.randn((1, HIDDEN), device="cuda").half()
@@ -221,8 +221,8 @@ class Stack:
         seed = 1000 * rank
         groups = [g for _ in range(LAYERS) for g in stack_groups()] + [("head", S.Q6_K, HIDDEN, VOCAB, "h")]
         for name, q, K, N, inp in groups:
-            assert N % world == 0
-            n = N // world
+            r0, r1 = shard.row_range(N, world, rank)  # this rank's output rows (vkflame_b200/shard.py)
+            n = r1 - r0
             seed += 1
             w = make_quant_weight_gpu(q, n, K, seed)
             y = torch.empty((1, n), device="cuda", dtype=torch.float16)
