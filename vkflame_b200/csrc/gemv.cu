@@ -53,6 +53,7 @@ __device__ unsigned long long g_timing[512][32][8];
 constexpr int NST_MAX = 8;            // ring depth cap
 constexpr int ROW_BUDGET = 4400;      // max bytes of one row per item
 constexpr int SMEM_MAX = 227 * 1024;
+constexpr int SMEM_HALF = 112 * 1024;  // two CTAs per SM
 constexpr int X_BUDGET = 120 * 1024;  // resident activations + sums
 constexpr int MAX_SLOTS = NST_MAX + 2; // per-warp row-block partial slots
 
@@ -98,13 +99,13 @@ __device__ __forceinline__ void store_y(const Args &a, int m, int n, float v) {
 }
 
 // Resident activations: one thread per (column, 32-value sub-block) reads the
-// 64 source bytes, stores them in fragment order (groups of four permuted
-// (x0, x2, x1, x3); owned layout: swizzled granules) and, for the K-quants,
-// their fp32 sum: split into hi + lo fp16 in the min-term MMA's B layout
-// [super-block][t] = (hi 2t, hi 2t+1, lo 2t, lo 2t+1), or (M = 1 column
-// form) as fp32 in the [super-block][t][2] order of the thread's sub-blocks.
-// SUMS: 0 none; 1 K-quant hi + lo fp16 (min-term MMA); 2 K-quant fp32 in
-// the column form's [t][2] order; 3 fp32 per 16-value group (Q6_K column form).
+// 64 source bytes and stores them in fragment order (groups of four permuted
+// (x0, x2, x1, x3); owned layout: swizzled granules) with, for the K-quants,
+// their fp32 sum split into hi + lo fp16 in the min-term MMA's B layout
+// [super-block][t] = (hi 2t, hi 2t+1, lo 2t, lo 2t+1).  The column forms
+// (M = 1) store integer activations instead (SUMS 4, 5).
+// SUMS: 0 none; 1 K-quant hi + lo fp16 (min-term MMA); 4 K-quant and 5 Q6_K
+// column forms (integer activations, below).
 template <bool OWN, int SUMS, int NTC>
 __device__ __forceinline__ void load_activations(const Args &a, uint8_t *xs, uint8_t *sums) {
     const int nsb = a.K / 32, jobs = a.M * nsb;
@@ -114,6 +115,64 @@ __device__ __forceinline__ void load_activations(const Args &a, uint8_t *xs, uin
         uint4 v[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) v[c] = __ldg(src + c);
+        if constexpr (SUMS >= 4) {
+            // Integer column forms (StepK1i, StepQ6i): 16-bit fixed point per
+            // 32-value run, x = s * (256 xh + xl), s = max|x| / 32639 (so xh,
+            // xl fit int8), stored in value order: xh at +0, xl at +256 of the
+            // unit; run scale and sum (and, Q6_K, the two 16-value group sums)
+            // in the unit's float area.
+            float f[32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 p = __half22float2(*reinterpret_cast<const __half2 *>(&w[e]));
+                    f[8 * c + 2 * e] = p.x;
+                    f[8 * c + 2 * e + 1] = p.y;
+                }
+            }
+            float amax = 0.f, s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+                amax = fmaxf(amax, fabsf(f[k]));
+                if (k < 16) s0 += f[k];
+                else s1 += f[k];
+            }
+            const float inv = amax > 0.f ? 32639.0f / amax : 0.f;
+            uint32_t hw[8], lw[8];
+#pragma unroll
+            for (int k4 = 0; k4 < 8; ++k4) {
+                uint32_t hb = 0, lb = 0;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int q = max(-32639, min(32639, __float2int_rn(f[4 * k4 + e] * inv)));
+                    const int h = (q + 128) >> 8, l = q - (h << 8);
+                    hb |= (uint32_t)(h & 0xFF) << (8 * e);
+                    lb |= (uint32_t)(l & 0xFF) << (8 * e);
+                }
+                hw[k4] = hb;
+                lw[k4] = lb;
+            }
+            uint8_t *run = xs + m * a.xpr + (sb / 8) * 512 + (sb % 8) * 32;
+            reinterpret_cast<uint4 *>(run)[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            reinterpret_cast<uint4 *>(run)[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+            reinterpret_cast<uint4 *>(run + 256)[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            reinterpret_cast<uint4 *>(run + 256)[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+            const float sc = amax / 32639.0f;
+            const int jj = sb % 8;
+            if constexpr (SUMS == 4) {
+                float *o = reinterpret_cast<float *>(sums + m * a.xsp + (sb / 8) * 64);
+                o[m1_sum_slot(jj)] = sc;
+                o[8 + m1_sum_slot(jj)] = s0 + s1;
+            } else {
+                float *o = reinterpret_cast<float *>(sums + m * a.xsp + (sb / 8) * 96);
+                o[jj] = sc;
+                o[8 + 2 * jj] = s0;
+                o[8 + 2 * jj + 1] = s1;
+            }
+            continue;
+        }
         uint8_t *col = xs + m * a.xpr;
         const int v0 = sb * 32;
 #pragma unroll
@@ -141,17 +200,7 @@ __device__ __forceinline__ void load_activations(const Args &a, uint8_t *xs, uin
                 }
                 part[c] = s2;
             }
-            if constexpr (SUMS == 3) {
-                float *o = reinterpret_cast<float *>(sums + m * a.xsp + (sb / 8) * 64) + 2 * (sb % 8);
-                o[0] = part[0] + part[1];
-                o[1] = part[2] + part[3];
-                continue;
-            }
             const float sum = (part[0] + part[1]) + (part[2] + part[3]);
-            if constexpr (SUMS == 2) {
-                reinterpret_cast<float *>(sums + m * a.xsp + (sb / 8) * 32)[m1_sum_slot(sb % 8)] = sum;
-                continue;
-            }
             const __half hi = __float2half_rn(sum);
             const __half lo = __float2half_rn(sum - __half2float(hi));
             __half *o = reinterpret_cast<__half *>(sums + m * a.xsp + (sb / 8) * 32 + ((sb % 8) / 2) * 8) + (sb & 1);
@@ -163,16 +212,16 @@ __device__ __forceinline__ void load_activations(const Args &a, uint8_t *xs, uin
 
 // Slot arithmetic shared by consumers and the reducer: row block number k of
 // this CTA (k = 0, 1, ...) uses slot k % slots, phase (k / slots) & 1.
-template <int QT, int CW, bool M1>
-__global__ void __launch_bounds__(32 * (CW + 2), 1) gemv_kernel(const __grid_constant__ Args a) {
+template <int QT, int CW, bool M1, int CPS>
+__global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_constant__ Args a) {
     constexpr int NTC = 32 * CW;
     constexpr int QK = Fmt<QT>::QK, BB = Fmt<QT>::BB;
     constexpr int UB = (256 / QK) * BB;  // bytes of one 256-value unit of a row
     constexpr bool KQ = QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K;
     constexpr bool OWN = Step<QT>::OWNED;
     constexpr bool Q6 = QT == VKF_DEQUANT_Q6_K;
-    constexpr bool COLS = M1 && (KQ || Q6);  // column-form decode (StepK1, StepQ6c)
-    constexpr int SUMS = COLS ? (KQ ? 2 : 3) : (KQ ? 1 : 0);
+    constexpr bool COLS = M1 && (KQ || Q6);  // column-form decode (StepK1i, StepQ6i)
+    constexpr int SUMS = COLS ? (KQ ? 4 : 5) : (KQ ? 1 : 0);
     constexpr int PW = COLS ? 2 : 4;         // parked floats per lane
     constexpr int PRODUCER = CW, REDUCER = CW + 1;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -358,10 +407,14 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1) gemv_kernel(const __grid_con
     const long long tp0 = clock64();
 #endif
     asm volatile("griddepcontrol.wait;" ::: "memory");
+#ifdef VKF_GEMV_TIMING
+    if (lane == 0) VKF_TACC(6, tp0);
+    const long long tx0 = clock64();
+#endif
     load_activations<OWN, SUMS, NTC>(a, xs, sums);
     consumer_bar<CW>();
 #ifdef VKF_GEMV_TIMING
-    if (lane == 0) VKF_TACC(2, tp0);
+    if (lane == 0) VKF_TACC(2, tx0);
     const long long tl0 = clock64();
     struct TEnd {
         long long t;
@@ -413,8 +466,8 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1) gemv_kernel(const __grid_con
             auto unit_step = [&](int uu) {
                 const int unit = u0 + uu;
                 if constexpr (COLS && KQ) {
-                    StepK1<QT == VKF_DEQUANT_Q5_K>::run(ra + uu * UB, rb + uu * UB, xs + unit * 512, g == t, g == t + 4,
-                                                        reinterpret_cast<const float *>(sums + unit * 32), t, acc);
+                    StepK1i<QT == VKF_DEQUANT_Q5_K>::run(ra + uu * UB, rb + uu * UB, xs + unit * 512, g == t, g == t + 4,
+                                                         reinterpret_cast<const float *>(sums + unit * 64), t, acc);
                 } else {
                     const int nblk = QK == 32 ? min(8, (a.K - unit * 256) / 32) : 8;
                     Step<QT>::run(ra + uu * UB, rb + uu * UB, xg + unit * 512, sg + unit * 32, t, nblk, acc);
@@ -427,9 +480,9 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1) gemv_kernel(const __grid_con
                 for (; u < nu; u += CW) {
                     const int unit = u0 + u;
                     const uint8_t *pa = ra + u * UB, *pb = rb + u * UB;
-                    const float *x16 = reinterpret_cast<const float *>(sums + unit * 64);
-                    if ((((uintptr_t)pa | (uintptr_t)pb) & 3) == 0) StepQ6c::run<true>(pa, pb, xs + unit * 512, g, x16, t, acc);
-                    else StepQ6c::run<false>(pa, pb, xs + unit * 512, g, x16, t, acc);
+                    const float *sx = reinterpret_cast<const float *>(sums + unit * 96);
+                    if ((((uintptr_t)pa | (uintptr_t)pb) & 3) == 0) StepQ6i::run<true>(pa, pb, xs + unit * 512, g, sx, t, acc);
+                    else StepQ6i::run<false>(pa, pb, xs + unit * 512, g, sx, t, acc);
                 }
             } else {
                 for (; u < nu; u += CW) unit_step(u);
@@ -507,7 +560,7 @@ static int pitch_conflicts(int64_t pitch, bool owned) {
     return worst;
 }
 
-template <int QT, int CW, bool M1>
+template <int QT, int CW, bool M1, int CPS>
 struct Launcher {
     static constexpr int QK = Fmt<QT>::QK, BB = Fmt<QT>::BB;
     static constexpr int UB = (256 / QK) * BB;
@@ -515,7 +568,10 @@ struct Launcher {
     static constexpr bool OWN = Step<QT>::OWNED;
     static constexpr int NT = 32 * (CW + 2);
 
-    static int launch(Args &a, int sms, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap) {
+    // require_whole: plan only (return VKF_ERR_UNSUPPORTED without launching)
+    // unless every item is a whole row block with at least two ring stages.
+    static int launch(Args &a, int sms, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap,
+                      bool require_whole = false) {
         auto up = [](int64_t v, int64_t m) { return (v + m - 1) / m * m; };
         a.units = (a.K + 255) / 256;
         // Column pitches: the owned layout's 16-byte fragment loads want
@@ -523,7 +579,7 @@ struct Launcher {
         // 8-byte loads 32 bytes.
         a.xpr = (int)up((int64_t)a.units * 512, 128) + (OWN ? 64 : 32);
         constexpr bool Q6 = QT == VKF_DEQUANT_Q6_K;
-        a.xsp = (M1 && Q6) ? a.units * 64 : KQ ? (int)up((int64_t)a.units * 32, 16) : 0;
+        a.xsp = (M1 && Q6) ? a.units * 96 : (M1 && KQ) ? a.units * 64 : KQ ? (int)up((int64_t)a.units * 32, 16) : 0;
         a.off_sums = a.M * a.xpr;
         const int x_end = (int)up(a.off_sums + (int64_t)a.M * a.xsp, 128);
         if (x_end > X_BUDGET) return VKF_ERR_UNSUPPORTED;
@@ -531,7 +587,8 @@ struct Launcher {
         constexpr bool COLS = M1 && (KQ || QT == VKF_DEQUANT_Q6_K);
         const int slot_bytes = CW * 32 * (COLS ? 2 : 4) * 4;
         const int bar_bytes = 2 * NST_MAX * 8 + 2 * MAX_SLOTS * 8;
-        const int avail = SMEM_MAX - x_end - bar_bytes - 128;
+        const int smem_cap = CPS == 2 ? SMEM_HALF : SMEM_MAX;
+        const int avail = smem_cap - x_end - bar_bytes - 128;
         a.T = (a.N + 15) / 16;
 
         // Units per item: whole rows when a row fits the budget (a 16-row
@@ -556,6 +613,7 @@ struct Launcher {
             a.upi = (a.units + a.S - 1) / a.S;
         }
         if (a.nst < 2) return VKF_ERR_UNSUPPORTED;
+        if (require_whole && !a.whole_tiles) return VKF_ERR_UNSUPPORTED;
         if ((int64_t)a.T * a.S > (int64_t)1 << 30) return VKF_ERR_UNSUPPORTED;
         a.I = a.T * a.S;
         a.slots = a.nst + 2;
@@ -568,10 +626,10 @@ struct Launcher {
         int dev = 0;
         cudaGetDevice(&dev);
         if (dev < 64 && !attr_set[dev]) {
-            cudaFuncSetAttribute(gemv_kernel<QT, CW, M1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX);
+            cudaFuncSetAttribute(gemv_kernel<QT, CW, M1, CPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_cap);
             attr_set[dev] = true;
         }
-        a.G = std::max(1, std::min(sms, a.I));
+        a.G = std::max(1, std::min(CPS * sms, a.I));
         if ((size_t)a.G * 2 * rows16m > ws_cap || (size_t)a.T > cnt_cap) return VKF_ERR_INVALID;
         a.ws = ws;
         a.cnt = cnt;
@@ -585,20 +643,32 @@ struct Launcher {
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        cudaLaunchKernelEx(&cfg, gemv_kernel<QT, CW, M1>, a);
+        cudaLaunchKernelEx(&cfg, gemv_kernel<QT, CW, M1, CPS>, a);
         return check_launch();
     }
 };
 
 // 8 consumer warps: with 16, each warp decodes fewer units per item and the
 // per-item overhead grows faster than the latency hiding gains (measured).
+// 8 consumer warps: with 16, each warp decodes fewer units per item and the
+// per-item overhead grows faster than the latency hiding gains (measured).
 constexpr int CW_DEFAULT = 8;
 
+// M = 1 K-quant and Q6_K launches use the column form.  Two CTAs per SM
+// (half the shared memory each) where whole row blocks still fit two ring
+// stages: a CTA of the next kernel on the stream can then start, and stream
+// its weights, as soon as either CTA of this one finishes (measured ~12 %
+// faster on the 14B stack's Q4_K shapes); otherwise one CTA per SM.
 template <int QT>
 static int launch_q(Args &a, int sms, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap) {
     constexpr bool COLS_FMT = QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K || QT == VKF_DEQUANT_Q6_K;
-    if (COLS_FMT && a.M == 1) return Launcher<QT, CW_DEFAULT, true>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    return Launcher<QT, CW_DEFAULT, false>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    if (COLS_FMT && a.M == 1) {
+        Args b = a;
+        const int rc = Launcher<QT, CW_DEFAULT, true, 2>::launch(b, sms, stream, ws, ws_cap, cnt, cnt_cap, true);
+        if (rc != VKF_ERR_UNSUPPORTED) return rc;
+        return Launcher<QT, CW_DEFAULT, true, 1>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    }
+    return Launcher<QT, CW_DEFAULT, false, 1>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
 }
 
 static int dispatch(int wtype, Args &a, int sms, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt,

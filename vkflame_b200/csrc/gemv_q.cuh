@@ -268,22 +268,13 @@ template <bool Q5> struct StepK {
     }
 };
 
-// M = 1 form of the K-quant decode.  With one activation column, seven of
-// the MMA's eight B columns would be idle; here they carry the sub-blocks.
-// Lane (g', t) supplies its activation fragment only in column g' = t (low
-// nibble MMAs) or g' = 4 + t (high nibble MMAs) and zero registers elsewhere
-// (a predicated-off load costs no shared-memory bandwidth), so
-// column t of every low MMA accumulates thread t's sub-block 2t and column
-// 4 + t of every high MMA sub-block 2t+1.  The A operand is the raw
-// "1024 + q" / "1024 + 16q" code (no fp16 scaling); after the super-block's
-// 16 MMAs each column holds  1024 * X_j + f_j * sum_l q_l x_l  exactly up to
-// fp32 accumulation (X_j the sub-block's activation sum, f_j = 1 or 16), and
-// thread (g, t), which owns columns 2t and 2t+1 (sub-blocks j1 = 4(t & 1) +
-// t / 2 and j1 + 2), applies
-//     acc += (d*sc_j/f_j) * D_j - (1024 * d*sc_j/f_j + dmin*m_j) * X_j.
-// The per-column sums are folded into one value per row at the end of the
-// row block (finish).
-__host__ __device__ __forceinline__ int m1_first_sub(int t) { return 4 * (t & 1) + (t >> 1); }
+// M = 1 column forms.  With one activation column, seven of the MMA's eight
+// B columns would be idle; instead they carry scale groups: a lane supplies
+// its activation fragment only in the column assigned to its own values and
+// zero registers elsewhere (a predicated-off load costs no shared-memory
+// bandwidth), so each column of the accumulator sums one scale group, and the
+// scales, mins and offsets are applied once per group in fp32 instead of to
+// every weight.  The codes enter the MMA as raw integers.
 // Position (t, e) of sub-block j in the per-super-block sums [t][e] (floats).
 __host__ __device__ __forceinline__ int m1_sum_slot(int j) {
     const int e = (j >> 1) & 1, b = j - 2 * e;  // b in {0, 1, 4, 5}
@@ -291,98 +282,19 @@ __host__ __device__ __forceinline__ int m1_sum_slot(int j) {
     return 2 * t + e;
 }
 
-template <bool Q5> struct StepK1 {
-    static constexpr bool OWNED = true;
-    __device__ __forceinline__ static float byte_f(uint32_t w, uint32_t b) {
-        return __uint_as_float(prmt(w, 0x4B000000u, b | 0x7540u)) - 8388608.0f;  // [w.b, 0, 0, 0x4B]
-    }
-    // xu: the unit's activations; lo_on / hi_on: this lane feeds column t /
-    // 4 + t (the other lanes' fragments are zero registers, not loads).
-    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xu, bool lo_on,
-                                               bool hi_on, const float *xs, int t, float (&acc)[4]) {
-        constexpr int QS = Q5 ? 48 : 16;
-        const uint4 hA = lds128(ra), hB = lds128(rb);
-        uint32_t wa[8], wb[8];
-        {
-            const uint4 a0 = lds128(ra + QS + 32 * t), a1 = lds128(ra + QS + 16 + 32 * t);
-            const uint4 b0 = lds128(rb + QS + 32 * t), b1 = lds128(rb + QS + 16 + 32 * t);
-            wa[0] = a0.x; wa[1] = a0.y; wa[2] = a0.z; wa[3] = a0.w; wa[4] = a1.x; wa[5] = a1.y; wa[6] = a1.z; wa[7] = a1.w;
-            wb[0] = b0.x; wb[1] = b0.y; wb[2] = b0.z; wb[3] = b0.w; wb[4] = b1.x; wb[5] = b1.y; wb[6] = b1.z; wb[7] = b1.w;
-        }
-        uint32_t ha[8], hb[8];
-        if constexpr (Q5) {
-            const uint4 a0 = lds128(ra + 16), a1 = lds128(ra + 32), b0 = lds128(rb + 16), b1 = lds128(rb + 32);
-            ha[0] = a0.x; ha[1] = a0.y; ha[2] = a0.z; ha[3] = a0.w; ha[4] = a1.x; ha[5] = a1.y; ha[6] = a1.z; ha[7] = a1.w;
-            hb[0] = b0.x; hb[1] = b0.y; hb[2] = b0.z; hb[3] = b0.w; hb[4] = b1.x; hb[5] = b1.y; hb[6] = b1.z; hb[7] = b1.w;
-        }
-        float D0[4] = {0.f, 0.f, 0.f, 0.f}, D1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-            uint4 xl = make_uint4(0, 0, 0, 0), xh = make_uint4(0, 0, 0, 0);
-            if (lo_on) xl = lds128(xu + owned_group_offset(64 * t + 4 * i));
-            if (hi_on) xh = lds128(xu + owned_group_offset(64 * t + 32 + 4 * i));
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const uint32_t a = wa[i + e], b = wb[i + e], a8 = a >> 8, b8 = b >> 8;
-                uint32_t AL[4] = {lop3_and_or(a, 0x000F000Fu, H2_MAGIC), lop3_and_or(b, 0x000F000Fu, H2_MAGIC),
-                                  lop3_and_or(a8, 0x000F000Fu, H2_MAGIC), lop3_and_or(b8, 0x000F000Fu, H2_MAGIC)};
-                uint32_t AH[4] = {lop3_and_or(a, 0x00F000F0u, H2_MAGIC), lop3_and_or(b, 0x00F000F0u, H2_MAGIC),
-                                  lop3_and_or(a8, 0x00F000F0u, H2_MAGIC), lop3_and_or(b8, 0x00F000F0u, H2_MAGIC)};
-                if constexpr (Q5) {
-                    const uint32_t qa = ha[i + e], qb = hb[i + e];
-                    const int s = 2 * t;
-                    AL[0] = lop3_and_or(s <= 4 ? qa << (4 - s) : qa >> (s - 4), 0x00100010u, AL[0]);
-                    AL[1] = lop3_and_or(s <= 4 ? qb << (4 - s) : qb >> (s - 4), 0x00100010u, AL[1]);
-                    AL[2] = lop3_and_or(qa >> (4 + s), 0x00100010u, AL[2]);
-                    AL[3] = lop3_and_or(qb >> (4 + s), 0x00100010u, AL[3]);
-                    AH[0] = lop3_and_or(qa << (7 - s), 0x01000100u, AH[0]);
-                    AH[1] = lop3_and_or(qb << (7 - s), 0x01000100u, AH[1]);
-                    AH[2] = lop3_and_or(qa >> (s + 1), 0x01000100u, AH[2]);
-                    AH[3] = lop3_and_or(qb >> (s + 1), 0x01000100u, AH[3]);
-                }
-                float (&D)[4] = e ? D1 : D0;
-                mma_16816(D, AL, e ? xl.z : xl.x, e ? xl.w : xl.y);
-                mma_16816(D, AH, e ? xh.z : xh.x, e ? xh.w : xh.y);
-            }
-        }
-        // Scales of the thread's sub-blocks j1, j1 + 2 for both rows.
-        const uint32_t b1 = (uint32_t)(t >> 1), b2 = b1 + 2;
-        const bool hi_sb = t >= 2;  // columns 4..7: high-nibble sub-blocks (codes carry 16q)
-        const float2 xv = *reinterpret_cast<const float2 *>(xs + 2 * t);
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const uint4 h = r ? hB : hA;
-            uint32_t scw, mw;
-            if (t & 1) {  // sub-blocks 4..7
-                scw = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
-                mw = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-            } else {
-                scw = h.y & 0x3F3F3F3Fu;
-                mw = h.z & 0x3F3F3F3Fu;
-            }
-            const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(&h.x));
-            const float df = hi_sb ? dd.x * 0.0625f : dd.x;
-            const float s1a = df * byte_f(scw, b1), s1b = df * byte_f(scw, b2);
-            const float c2a = fmaf(1024.0f, s1a, dd.y * byte_f(mw, b1));
-            const float c2b = fmaf(1024.0f, s1b, dd.y * byte_f(mw, b2));
-            float &o0 = acc[2 * r], &o1 = acc[2 * r + 1];
-            o0 = fmaf(-c2a, xv.x, fmaf(s1a, D0[2 * r] + D1[2 * r], o0));
-            o1 = fmaf(-c2b, xv.y, fmaf(s1b, D0[2 * r + 1] + D1[2 * r + 1], o1));
-        }
-    }
-    // Row block end: fold the 8 sub-block columns into column 0 (lanes t = 0).
-    __device__ __forceinline__ static void finish(float (&acc)[4]) {
-        float r0 = acc[0] + acc[1], r1 = acc[2] + acc[3];
-        r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
-        r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
-        r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
-        r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
-        acc[0] = r0;
-        acc[1] = 0.f;
-        acc[2] = r1;
-        acc[3] = 0.f;
-    }
-};
+// Row block end of a column form: each lane holds columns 2t, 2t+1 of rows
+// g, g+8; fold the eight columns into column 0 (lanes t = 0).
+__device__ __forceinline__ void fold_columns(float (&acc)[4]) {
+    float r0 = acc[0] + acc[1], r1 = acc[2] + acc[3];
+    r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
+    r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
+    r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
+    r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
+    acc[0] = r0;
+    acc[1] = 0.f;
+    acc[2] = r1;
+    acc[3] = 0.f;
+}
 
 template <> struct Step<VKF_DEQUANT_Q4_K> : StepK<false> {};
 template <> struct Step<VKF_DEQUANT_Q5_K> : StepK<true> {};
@@ -437,68 +349,168 @@ template <int IP> struct StepQ6 {
     }
 };
 
-// Q6_K, M = 1 column form (see StepK1): the MMA of (ip, s, h) covers the 16
-// values of scale group 8 ip + 2 s + h (plain mapping: thread t holds
-// l = 16 h + 4 t .. + 3), and only lanes of column c = 2 s + h supply
-// activations, so after the 8 MMAs of half ip column c holds group
-// 8 ip + c:  D = 1024 X16 + f sum q x  with A the raw code "1024 + q" (s < 2,
-// f = 1) or "1024 + 16 q" (s >= 2, f = 16).  Thread (g, t) owns columns 2t and
-// 2t+1 (s = t, h = 0 / 1) and adds  d*sc * (D / f - (1024 / f + 32) * X16)
-// (the value is d*sc*(q - 32), dequant_q6_k.glsl:34-58).  The 6-bit codes are
-// built from one ql and one qh word per MMA with shifts shared by the four s:
-// qh << 4 places bits 0-1 at 4-5 (s = 0) and bits 4-5 at 8-9 (s = 2), qh << 2
-// serves s = 1 and s = 3, and >> 4 / >> 6 the same for bytes 1 and 3.
-// Super-blocks are 210 bytes: words of odd ones start 2 mod 4 and are read as
-// two aligned words and a byte permute (AL4 = false).
-struct StepQ6c {
-    static constexpr bool OWNED = false;
+// Q4_K and Q5_K, M = 1 column form (owned mapping: thread t holds the quant
+// bytes 32t .. 32t + 31, sub-blocks 2t (low nibbles) and 2t + 1 (high)).
+// The activations are 16-bit fixed point per 32-value sub-block,
+// x = s_j * (256 * xh + xl) with xh, xl int8, and the codes enter
+// `mma.sync.m16n8k32.s8` as raw int8 (one LOP3 makes four codes:
+// q & 0x0F0F0F0F, (q >> 4) & 0x0F0F0F0F).  Lane (g', t) feeds its
+// activations only into column t (low nibbles, sub-block 2t) or 4 + t (high
+// nibbles, 2t + 1); thread (g, t) then owns columns 2t, 2t + 1 = sub-blocks
+// j1 = 4 (t & 1) + t / 2 and j1 + 2.  Per sub-block and row the int32 sums
+// are exact (|D| < 2^24 for Q4_K); the thread applies
+//     acc += d*sc_j*s_j * (256 Dh + Dl) - dmin*m_j * X_j.
+// Activation layout per super-block: xh[256] | xl[256] (int8, value order),
+// then per sub-block s_j (fp32) in [t][2] order, X_j (fp32) in [t][2] order.
+__device__ __forceinline__ void mma_16832_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <bool Q5> struct StepK1i {
+    static constexpr bool OWNED = true;
+    __device__ __forceinline__ static float byte_f(uint32_t w, uint32_t b) {
+        return __uint_as_float(prmt(w, 0x4B000000u, b | 0x7540u)) - 8388608.0f;
+    }
+    // xu: the unit's 512 activation bytes; sx: the unit's [s (8 floats) | X (8 floats)].
+    __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xu, bool lo_on,
+                                               bool hi_on, const float *sx, int t, float (&acc)[4]) {
+        constexpr int QS = Q5 ? 48 : 16;
+        const uint4 hA = lds128(ra), hB = lds128(rb);
+        uint32_t wa[8], wb[8];
+        {
+            const uint4 a0 = lds128(ra + QS + 32 * t), a1 = lds128(ra + QS + 16 + 32 * t);
+            const uint4 b0 = lds128(rb + QS + 32 * t), b1 = lds128(rb + QS + 16 + 32 * t);
+            wa[0] = a0.x; wa[1] = a0.y; wa[2] = a0.z; wa[3] = a0.w; wa[4] = a1.x; wa[5] = a1.y; wa[6] = a1.z; wa[7] = a1.w;
+            wb[0] = b0.x; wb[1] = b0.y; wb[2] = b0.z; wb[3] = b0.w; wb[4] = b1.x; wb[5] = b1.y; wb[6] = b1.z; wb[7] = b1.w;
+        }
+        uint32_t ha[8], hb[8];
+        if constexpr (Q5) {
+            const uint4 a0 = lds128(ra + 16), a1 = lds128(ra + 32), b0 = lds128(rb + 16), b1 = lds128(rb + 32);
+            ha[0] = a0.x; ha[1] = a0.y; ha[2] = a0.z; ha[3] = a0.w; ha[4] = a1.x; ha[5] = a1.y; ha[6] = a1.z; ha[7] = a1.w;
+            hb[0] = b0.x; hb[1] = b0.y; hb[2] = b0.z; hb[3] = b0.w; hb[4] = b1.x; hb[5] = b1.y; hb[6] = b1.z; hb[7] = b1.w;
+        }
+        int Dh[4] = {0, 0, 0, 0}, Dl[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+            // B: 8 consecutive int8 of the thread's values (64t + 4i .. +7, low; +32, high)
+            uint2 lh = make_uint2(0, 0), ll = make_uint2(0, 0), hh = make_uint2(0, 0), hl = make_uint2(0, 0);
+            if (lo_on) {
+                lh = *reinterpret_cast<const uint2 *>(xu + 64 * t + 4 * i);
+                ll = *reinterpret_cast<const uint2 *>(xu + 256 + 64 * t + 4 * i);
+            }
+            if (hi_on) {
+                hh = *reinterpret_cast<const uint2 *>(xu + 64 * t + 32 + 4 * i);
+                hl = *reinterpret_cast<const uint2 *>(xu + 256 + 64 * t + 32 + 4 * i);
+            }
+            uint32_t AL[4] = {wa[i] & 0x0F0F0F0Fu, wb[i] & 0x0F0F0F0Fu, wa[i + 1] & 0x0F0F0F0Fu, wb[i + 1] & 0x0F0F0F0Fu};
+            uint32_t AH[4] = {(wa[i] >> 4) & 0x0F0F0F0Fu, (wb[i] >> 4) & 0x0F0F0F0Fu, (wa[i + 1] >> 4) & 0x0F0F0F0Fu,
+                              (wb[i + 1] >> 4) & 0x0F0F0F0Fu};
+            if constexpr (Q5) {
+                // fifth bit: qh[l] bit 2t (low) / 2t + 1 (high) -> code bit 4 of each byte
+                const int s = 2 * t;
+                AL[0] |= ((ha[i] >> s) & 0x01010101u) << 4;
+                AL[1] |= ((hb[i] >> s) & 0x01010101u) << 4;
+                AL[2] |= ((ha[i + 1] >> s) & 0x01010101u) << 4;
+                AL[3] |= ((hb[i + 1] >> s) & 0x01010101u) << 4;
+                AH[0] |= ((ha[i] >> (s + 1)) & 0x01010101u) << 4;
+                AH[1] |= ((hb[i] >> (s + 1)) & 0x01010101u) << 4;
+                AH[2] |= ((ha[i + 1] >> (s + 1)) & 0x01010101u) << 4;
+                AH[3] |= ((hb[i + 1] >> (s + 1)) & 0x01010101u) << 4;
+            }
+            mma_16832_s8(Dh, AL, lh.x, lh.y);
+            mma_16832_s8(Dl, AL, ll.x, ll.y);
+            mma_16832_s8(Dh, AH, hh.x, hh.y);
+            mma_16832_s8(Dl, AH, hl.x, hl.y);
+        }
+        const uint32_t b1 = (uint32_t)(t >> 1), b2 = b1 + 2;
+        const float2 sj = *reinterpret_cast<const float2 *>(sx + 2 * t);
+        const float2 xj = *reinterpret_cast<const float2 *>(sx + 8 + 2 * t);
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const uint4 h = r ? hB : hA;
+            uint32_t scw, mw;
+            if (t & 1) {
+                scw = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+                mw = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+            } else {
+                scw = h.y & 0x3F3F3F3Fu;
+                mw = h.z & 0x3F3F3F3Fu;
+            }
+            const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(&h.x));
+            const float qa = (float)(256 * Dh[2 * r] + Dl[2 * r]), qb = (float)(256 * Dh[2 * r + 1] + Dl[2 * r + 1]);
+            float &o0 = acc[2 * r], &o1 = acc[2 * r + 1];
+            o0 = fmaf(dd.x * byte_f(scw, b1) * sj.x, qa, fmaf(-dd.y * byte_f(mw, b1), xj.x, o0));
+            o1 = fmaf(dd.x * byte_f(scw, b2) * sj.y, qb, fmaf(-dd.y * byte_f(mw, b2), xj.y, o1));
+        }
+    }
+};
+
+// Q6_K, M = 1 column form.  MMA (ip, s) (m16n8k32.s8) covers the 32
+// values l = 0..31 of run (ip, s); thread t holds l = 8t .. 8t + 7 (words e = 0,
+// 1), all in scale group h = t >> 1, so lanes of column c = 2s + (t >> 1)
+// feed activations and, after the four MMAs of half ip, column 2s + h holds
+// group 8 ip + 2s + h.  A = the 6-bit code q (0..63) byte-wise: nibble of
+// ql[64 ip + 32 (s & 1) + l] (low for s < 2, high for s >= 2) | qh bits 2s, 2s+1
+// moved to bits 4, 5 (dequant_q6_k.glsl:34-58).  Activations as for StepK1i
+// (x = s_j * (256 xh + xl) per 32-value run j = 4 ip + s); thread (g, t) owns
+// groups (ip, t, h) and adds  d * sc * (s_j * (256 Dh + Dl) - 32 * X16).
+// Odd super-blocks start 2 mod 4: their words are two aligned words and a
+// byte permute (AL4 = false).
+struct StepQ6i {
     template <bool AL4> __device__ __forceinline__ static uint32_t w32(const uint8_t *p) {
         if constexpr (AL4) return *reinterpret_cast<const uint32_t *>(p);
         const uint32_t lo = *reinterpret_cast<const uint32_t *>(p - 2), hi = *reinterpret_cast<const uint32_t *>(p + 2);
         return prmt(lo, hi, 0x5432);
     }
-    // Codes of value pair (bytes 0,2) [pair 0] or (1,3) [pair 1] for s.
-    template <int S>
-    __device__ __forceinline__ static uint32_t code(uint32_t ql, uint32_t ql8, uint32_t h4, uint32_t h2, uint32_t hr4,
-                                                    uint32_t hr6, int pair) {
-        constexpr uint32_t NM = S < 2 ? 0x000F000Fu : 0x00F000F0u, HM = S < 2 ? 0x00300030u : 0x03000300u;
-        const uint32_t q = pair ? ql8 : ql;
-        const uint32_t hh = pair ? ((S & 1) ? hr6 : hr4) : ((S & 1) ? h2 : h4);
-        return lop3_and_or(q, NM, lop3_and_or(hh, HM, H2_MAGIC));
+    template <int S> __device__ __forceinline__ static uint32_t code(uint32_t q0, uint32_t q1, uint32_t qh) {
+        const uint32_t ql = (S & 1) ? q1 : q0;
+        const uint32_t nib = S < 2 ? (ql & 0x0F0F0F0Fu) : ((ql >> 4) & 0x0F0F0F0Fu);
+        const uint32_t hs = S == 0 ? qh << 4 : S == 1 ? qh << 2 : S == 2 ? qh : qh >> 2;
+        return lop3_and_or(hs, 0x30303030u, nib);
     }
+    // xu: the unit's xh[256] | xl[256]; sx: s[8] (runs) | X16[16] (groups).
     template <bool AL4>
     __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xu, int g,
-                                               const float *x16, int t, float (&acc)[4]) {
+                                               const float *sx, int t, float (&acc)[4]) {
         const float da = half_bits_to_float(ld_u16(ra + 208)), db = half_bits_to_float(ld_u16(rb + 208));
-        const float f = t >= 2 ? 0.0625f : 1.0f, c32 = t >= 2 ? 96.0f : 1056.0f;
 #pragma unroll
         for (int ip = 0; ip < 2; ++ip) {
-            float D[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t a0[2], a1[2], ah[2], b0[2], b1[2], bh[2];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int o = 64 * ip + 16 * h + 4 * t, oh = 128 + 32 * ip + 16 * h + 4 * t;
-                const uint32_t a0 = w32<AL4>(ra + o), a1 = w32<AL4>(ra + o + 32), ah = w32<AL4>(ra + oh);
-                const uint32_t b0 = w32<AL4>(rb + o), b1 = w32<AL4>(rb + o + 32), bh = w32<AL4>(rb + oh);
-                const uint32_t a08 = a0 >> 8, a18 = a1 >> 8, b08 = b0 >> 8, b18 = b1 >> 8;
-                const uint32_t ah4 = ah << 4, ah2 = ah << 2, ahr4 = ah >> 4, ahr6 = ah >> 6;
-                const uint32_t bh4 = bh << 4, bh2 = bh << 2, bhr4 = bh >> 4, bhr6 = bh >> 6;
-#define VKF_Q6C_MMA(S, QA, QA8, QB, QB8)                                                                        \
-    {                                                                                                           \
-        const uint32_t A[4] = {code<S>(QA, QA8, ah4, ah2, ahr4, ahr6, 0), code<S>(QB, QB8, bh4, bh2, bhr4, bhr6, 0), \
-                               code<S>(QA, QA8, ah4, ah2, ahr4, ahr6, 1), code<S>(QB, QB8, bh4, bh2, bhr4, bhr6, 1)}; \
-        uint2 xv = make_uint2(0, 0);                                                                            \
-        if (g == 2 * S + h) xv = *reinterpret_cast<const uint2 *>(xu + (128 * ip + 32 * S + 16 * h + 4 * t) * 2); \
-        mma_16816(D, A, xv.x, xv.y);                                                                            \
-    }
-                VKF_Q6C_MMA(0, a0, a08, b0, b08)
-                VKF_Q6C_MMA(1, a1, a18, b1, b18)
-                VKF_Q6C_MMA(2, a0, a08, b0, b08)
-                VKF_Q6C_MMA(3, a1, a18, b1, b18)
-#undef VKF_Q6C_MMA
+            for (int e = 0; e < 2; ++e) {
+                const int o = 64 * ip + 8 * t + 4 * e, oh = 128 + 32 * ip + 8 * t + 4 * e;
+                a0[e] = w32<AL4>(ra + o);
+                a1[e] = w32<AL4>(ra + o + 32);
+                ah[e] = w32<AL4>(ra + oh);
+                b0[e] = w32<AL4>(rb + o);
+                b1[e] = w32<AL4>(rb + o + 32);
+                bh[e] = w32<AL4>(rb + oh);
             }
-            // Columns 2t, 2t+1 = groups 8 ip + 2t + h: int8 scales at 192 + 8 ip + 2t (+1).
+            int Dh[4] = {0, 0, 0, 0}, Dl[4] = {0, 0, 0, 0};
+#define VKF_Q6I_MMA(S)                                                                                   \
+    {                                                                                                    \
+        const uint32_t A[4] = {code<S>(a0[0], a1[0], ah[0]), code<S>(b0[0], b1[0], bh[0]),               \
+                               code<S>(a0[1], a1[1], ah[1]), code<S>(b0[1], b1[1], bh[1])};               \
+        uint2 xh = make_uint2(0, 0), xl = make_uint2(0, 0);                                              \
+        if (g == 2 * S + (t >> 1)) {                                                                     \
+            xh = *reinterpret_cast<const uint2 *>(xu + 128 * ip + 32 * S + 8 * t);                       \
+            xl = *reinterpret_cast<const uint2 *>(xu + 256 + 128 * ip + 32 * S + 8 * t);                 \
+        }                                                                                                \
+        mma_16832_s8(Dh, A, xh.x, xh.y);                                                                 \
+        mma_16832_s8(Dl, A, xl.x, xl.y);                                                                 \
+    }
+            VKF_Q6I_MMA(0)
+            VKF_Q6I_MMA(1)
+            VKF_Q6I_MMA(2)
+            VKF_Q6I_MMA(3)
+#undef VKF_Q6I_MMA
+            // Columns 2t, 2t+1 = groups 8 ip + 2t + h of run 4 ip + t.
             const uint32_t sa = ld_u16(ra + 192 + 8 * ip + 2 * t), sb = ld_u16(rb + 192 + 8 * ip + 2 * t);
-            const float2 xg = *reinterpret_cast<const float2 *>(x16 + 8 * ip + 2 * t);
+            const float sj = sx[4 * ip + t];
+            const float2 x16 = *reinterpret_cast<const float2 *>(sx + 8 + 8 * ip + 2 * t);
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
                 const uint32_t sw = r ? sb : sa;
@@ -506,8 +518,9 @@ struct StepQ6c {
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
                     const float dsc = d * (float)(int8_t)(sw >> (8 * hh));
+                    const float q = (float)(256 * Dh[2 * r + hh] + Dl[2 * r + hh]);
                     float &o = acc[2 * r + hh];
-                    o = fmaf(dsc * f, D[2 * r + hh], fmaf(-dsc * c32, hh ? xg.y : xg.x, o));
+                    o = fmaf(dsc * sj, q, fmaf(-32.0f * dsc, hh ? x16.y : x16.x, o));
                 }
             }
         }
