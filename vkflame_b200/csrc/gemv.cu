@@ -41,8 +41,18 @@ namespace vkf {
 namespace gemv {
 
 #ifdef VKF_GEMV_TIMING
-// Debug builds only: per-warp cycle counters [cta][warp][phase].
+// Debug builds only: per-warp cycle counters [cta][warp][phase], and per
+// launch the earliest CTA start / latest CTA end / earliest consumer start
+// after the dependency wait (global timer, ns).
 __device__ unsigned long long g_timing[512][32][8];
+__device__ unsigned long long g_timeline[4096][3];
+__device__ unsigned long long g_cta_t[4096][512][5];  // per launch, per CTA: start, dep, prologue, loop, reducer
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+static int g_launch_id = 0;
 #define VKF_T0() const long long _t0 = clock64()
 #define VKF_TACC(ph, t0) atomicAdd(&g_timing[blockIdx.x][threadIdx.x >> 5][ph], (unsigned long long)(clock64() - (t0)))
 #else
@@ -82,6 +92,9 @@ struct Args {
     int y_f16;
     int prefetch;      // stream weights before the previous kernel on the stream completes
     int whole_tiles;   // S == 1 and W 16-byte aligned: one copy per row block
+#ifdef VKF_GEMV_TIMING
+    int launch_id;
+#endif
 };
 
 __device__ __forceinline__ int first_item(int c, const Args &a) { return (int)((int64_t)c * a.I / a.G); }
@@ -104,73 +117,93 @@ __device__ __forceinline__ void store_y(const Args &a, int m, int n, float v) {
 // their fp32 sum split into hi + lo fp16 in the min-term MMA's B layout
 // [super-block][t] = (hi 2t, hi 2t+1, lo 2t, lo 2t+1).  The column forms
 // (M = 1) store integer activations instead (SUMS 4, 5).
+// Integer column forms (StepK1i, StepQ6i): 16-bit fixed point per 32-value
+// run, x = s * (256 xh + xl), s = max|x| / 32639 (so xh, xl fit int8), stored
+// in value order (xh at +0, xl at +256 of the unit); the run's scale and sum
+// (and, Q6_K, its two 16-value group sums) go to the unit's float area.
+template <int SUMS>
+__device__ __forceinline__ void quantize_run(const Args &a, const uint4 (&v)[4], int m, int sb, uint8_t *xs,
+                                             uint8_t *sums) {
+        // Integer column forms (StepK1i, StepQ6i): 16-bit fixed point per
+        // 32-value run, x = s * (256 xh + xl), s = max|x| / 32639 (so xh,
+        // xl fit int8), stored in value order: xh at +0, xl at +256 of the
+        // unit; run scale and sum (and, Q6_K, the two 16-value group sums)
+        // in the unit's float area.
+        float f[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 p = __half22float2(*reinterpret_cast<const __half2 *>(&w[e]));
+                f[8 * c + 2 * e] = p.x;
+                f[8 * c + 2 * e + 1] = p.y;
+            }
+        }
+        float amax = 0.f, s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+            amax = fmaxf(amax, fabsf(f[k]));
+            if (k < 16) s0 += f[k];
+            else s1 += f[k];
+        }
+        const float inv = amax > 0.f ? 32639.0f / amax : 0.f;
+        uint32_t hw[8], lw[8];
+#pragma unroll
+        for (int k4 = 0; k4 < 8; ++k4) {
+            uint32_t hb = 0, lb = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int q = max(-32639, min(32639, __float2int_rn(f[4 * k4 + e] * inv)));
+                const int h = (q + 128) >> 8, l = q - (h << 8);
+                hb |= (uint32_t)(h & 0xFF) << (8 * e);
+                lb |= (uint32_t)(l & 0xFF) << (8 * e);
+            }
+            hw[k4] = hb;
+            lw[k4] = lb;
+        }
+        uint8_t *run = xs + m * a.xpr + (sb / 8) * 512 + (sb % 8) * 32;
+        reinterpret_cast<uint4 *>(run)[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        reinterpret_cast<uint4 *>(run)[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+        reinterpret_cast<uint4 *>(run + 256)[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        reinterpret_cast<uint4 *>(run + 256)[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+        const float sc = amax / 32639.0f;
+        const int jj = sb % 8;
+        if constexpr (SUMS == 4) {
+            float *o = reinterpret_cast<float *>(sums + m * a.xsp + (sb / 8) * 64);
+            o[m1_sum_slot(jj)] = sc;
+            o[8 + m1_sum_slot(jj)] = s0 + s1;
+        } else {
+            float *o = reinterpret_cast<float *>(sums + m * a.xsp + (sb / 8) * 96);
+            o[jj] = sc;
+            o[8 + 2 * jj] = s0;
+            o[8 + 2 * jj + 1] = s1;
+        }
+        
+}
+
 // SUMS: 0 none; 1 K-quant hi + lo fp16 (min-term MMA); 4 K-quant and 5 Q6_K
 // column forms (integer activations, below).
 template <bool OWN, int SUMS, int NTC>
 __device__ __forceinline__ void load_activations(const Args &a, uint8_t *xs, uint8_t *sums) {
     const int nsb = a.K / 32, jobs = a.M * nsb;
-    for (int j = threadIdx.x; j < jobs; j += NTC) {
+    // Every CTA reads the same activations at the same moment: start each CTA
+    // at a different run so the requests spread over the row's L2 lines.
+    const int rot = (int)(((unsigned)blockIdx.x * 97u) % (unsigned)jobs);
+    for (int j0 = threadIdx.x; j0 < jobs; j0 += NTC) {
+        int j = j0 + rot;
+        if (j >= jobs) j -= jobs;
         const int m = j / nsb, sb = j - m * nsb;
         const uint4 *src = reinterpret_cast<const uint4 *>(a.X + (int64_t)m * a.ldx_bytes + sb * 64);
         uint4 v[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) v[c] = __ldg(src + c);
+#ifdef VKF_NOXLOAD  // debug experiment only: constant activations instead of loads
+#pragma unroll
+        for (int c = 0; c < 4; ++c) v[c] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
+#endif
         if constexpr (SUMS >= 4) {
-            // Integer column forms (StepK1i, StepQ6i): 16-bit fixed point per
-            // 32-value run, x = s * (256 xh + xl), s = max|x| / 32639 (so xh,
-            // xl fit int8), stored in value order: xh at +0, xl at +256 of the
-            // unit; run scale and sum (and, Q6_K, the two 16-value group sums)
-            // in the unit's float area.
-            float f[32];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 p = __half22float2(*reinterpret_cast<const __half2 *>(&w[e]));
-                    f[8 * c + 2 * e] = p.x;
-                    f[8 * c + 2 * e + 1] = p.y;
-                }
-            }
-            float amax = 0.f, s0 = 0.f, s1 = 0.f;
-#pragma unroll
-            for (int k = 0; k < 32; ++k) {
-                amax = fmaxf(amax, fabsf(f[k]));
-                if (k < 16) s0 += f[k];
-                else s1 += f[k];
-            }
-            const float inv = amax > 0.f ? 32639.0f / amax : 0.f;
-            uint32_t hw[8], lw[8];
-#pragma unroll
-            for (int k4 = 0; k4 < 8; ++k4) {
-                uint32_t hb = 0, lb = 0;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int q = max(-32639, min(32639, __float2int_rn(f[4 * k4 + e] * inv)));
-                    const int h = (q + 128) >> 8, l = q - (h << 8);
-                    hb |= (uint32_t)(h & 0xFF) << (8 * e);
-                    lb |= (uint32_t)(l & 0xFF) << (8 * e);
-                }
-                hw[k4] = hb;
-                lw[k4] = lb;
-            }
-            uint8_t *run = xs + m * a.xpr + (sb / 8) * 512 + (sb % 8) * 32;
-            reinterpret_cast<uint4 *>(run)[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            reinterpret_cast<uint4 *>(run)[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-            reinterpret_cast<uint4 *>(run + 256)[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-            reinterpret_cast<uint4 *>(run + 256)[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
-            const float sc = amax / 32639.0f;
-            const int jj = sb % 8;
-            if constexpr (SUMS == 4) {
-                float *o = reinterpret_cast<float *>(sums + m * a.xsp + (sb / 8) * 64);
-                o[m1_sum_slot(jj)] = sc;
-                o[8 + m1_sum_slot(jj)] = s0 + s1;
-            } else {
-                float *o = reinterpret_cast<float *>(sums + m * a.xsp + (sb / 8) * 96);
-                o[jj] = sc;
-                o[8 + 2 * jj] = s0;
-                o[8 + 2 * jj + 1] = s1;
-            }
+            quantize_run<SUMS>(a, v, m, sb, xs, sums);
             continue;
         }
         uint8_t *col = xs + m * a.xpr;
@@ -241,6 +274,14 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
     // its prologue now; everything this kernel reads or writes that another
     // kernel may touch (X, Y, the scratch) waits for the previous kernel.
     asm volatile("griddepcontrol.launch_dependents;");
+#ifdef VKF_GEMV_TIMING
+    unsigned long long gt0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(gt0));
+    if (threadIdx.x == 0 && a.launch_id < 4096) {
+        atomicMin(&g_timeline[a.launch_id][0], gt0);
+        g_cta_t[a.launch_id][blockIdx.x][0] = gt0;
+    }
+#endif
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.nst; ++s) {
             mbar_init(&full[s], 1);
@@ -399,6 +440,14 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
             }
             if (lane == 0) a.cnt[tb] = 0;
         }
+#ifdef VKF_GEMV_TIMING
+        if (lane == 0 && a.launch_id < 4096) {
+            unsigned long long ge;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ge));
+            atomicMax(&g_timeline[a.launch_id][1], ge);
+            g_cta_t[a.launch_id][blockIdx.x][4] = ge;
+        }
+#endif
         return;
     }
 
@@ -406,13 +455,33 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
 #ifdef VKF_GEMV_TIMING
     const long long tp0 = clock64();
 #endif
+    // Pull the activation rows into L2 while the previous kernel finishes.  A
+    // prefetch consumes no data (the loads below come after the dependency
+    // wait, and L2 is the point of coherence), so it is safe even when the
+    // previous kernel writes X; it only hides the DRAM latency of an X that
+    // has left L2.
+    for (int i = threadIdx.x; i < a.M * (int)((a.K * 2 + 127) / 128); i += NTC) {
+        const int m = i / ((a.K * 2 + 127) / 128), l = i - m * ((a.K * 2 + 127) / 128);
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a.X + (int64_t)m * a.ldx_bytes + l * 128));
+    }
     asm volatile("griddepcontrol.wait;" ::: "memory");
 #ifdef VKF_GEMV_TIMING
     if (lane == 0) VKF_TACC(6, tp0);
     const long long tx0 = clock64();
 #endif
+#ifdef VKF_GEMV_TIMING
+    if (threadIdx.x == 0 && a.launch_id < 4096) {
+        unsigned long long gw;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(gw));
+        atomicMin(&g_timeline[a.launch_id][2], gw);
+        g_cta_t[a.launch_id][blockIdx.x][1] = gw;
+    }
+#endif
     load_activations<OWN, SUMS, NTC>(a, xs, sums);
     consumer_bar<CW>();
+#ifdef VKF_GEMV_TIMING
+    if (threadIdx.x == 0 && a.launch_id < 4096) g_cta_t[a.launch_id][blockIdx.x][2] = gtimer();
+#endif
 #ifdef VKF_GEMV_TIMING
     if (lane == 0) VKF_TACC(2, tx0);
     const long long tl0 = clock64();
@@ -438,6 +507,9 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
     uint32_t ph = 0;
     int ubase = 0;  // units of this CTA's earlier items, mod CW
     int k = 0;      // row blocks finished by this CTA
+    int park_slot = 0;
+    uint32_t park_phase = 0;  // phase of the slot's current use
+    const int64_t row_off_a = (int64_t)g * a.row_bytes, row_off_b = (int64_t)(g + 8) * a.row_bytes;
     for (int it = it0; it < it1; ++it) {
 #ifdef VKF_GEMV_TIMING
         const long long tw0 = clock64();
@@ -452,8 +524,8 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
             const uint8_t *st = ring + s * a.stage_bytes;
             const uint8_t *ra, *rb;
             if (a.whole_tiles) {  // contiguous image of the row block
-                ra = st + g * a.row_bytes;
-                rb = ra + 8 * a.row_bytes;
+                ra = st + row_off_a;
+                rb = st + row_off_b;
             } else {
                 const int64_t row_a = (int64_t)tile * 16 + g;
                 const uintptr_t ga = (uintptr_t)a.W + row_a * a.row_bytes + (int64_t)u0 * UB;
@@ -516,11 +588,11 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
         // Park this warp's partial of the finished row block (one vector store
         // per lane) and signal the reducer; a slot is reused only after the
         // reducer has freed it (slots row blocks earlier).
-        const int sl = k % a.slots;
+        const int sl = park_slot;
 #ifdef VKF_GEMV_TIMING
         const long long tf0 = clock64();
 #endif
-        if (k >= a.slots && ok) ok = mbar_wait(&freed[sl], (uint32_t)(k / a.slots - 1) & 1u, a.err);
+        if (k >= a.slots && ok) ok = mbar_wait(&freed[sl], park_phase ^ 1u, a.err);
 #ifdef VKF_GEMV_TIMING
         if (lane == 0) VKF_TACC(4, tf0);
 #endif
@@ -534,7 +606,14 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
         __syncwarp();
         if (lane == 0) mbar_arrive(&parked[sl]);
         ++k;
+        if (++park_slot == a.slots) {
+            park_slot = 0;
+            park_phase ^= 1u;
+        }
     }
+#ifdef VKF_GEMV_TIMING
+    if (lane == 0 && a.launch_id < 4096) atomicMax(&g_cta_t[a.launch_id][blockIdx.x][3], gtimer());
+#endif
 }
 
 // Worst shared-memory bank multiplicity of the decode's weight loads when rows
@@ -643,6 +722,9 @@ struct Launcher {
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
+#ifdef VKF_GEMV_TIMING
+        a.launch_id = g_launch_id++;
+#endif
         cudaLaunchKernelEx(&cfg, gemv_kernel<QT, CW, M1, CPS>, a);
         return check_launch();
     }
@@ -686,6 +768,19 @@ static int dispatch(int wtype, Args &a, int sms, cudaStream_t stream, float *ws,
 }  // namespace gemv
 
 #ifdef VKF_GEMV_TIMING
+extern "C" int vkf_gemv_cta_times(void *host, int launch) {
+    return (int)cudaMemcpyFromSymbol(host, gemv::g_cta_t, sizeof(unsigned long long) * 512 * 5,
+                                     sizeof(unsigned long long) * 512 * 5 * (size_t)launch);
+}
+extern "C" int vkf_gemv_timeline(void *host, int reset) {
+    if (reset) {
+        static unsigned long long init[4096][3];
+        for (auto &r : init) { r[0] = ~0ull; r[1] = 0; r[2] = ~0ull; }
+        gemv::g_launch_id = 0;
+        return (int)cudaMemcpyToSymbol(gemv::g_timeline, init, sizeof(init));
+    }
+    return (int)cudaMemcpyFromSymbol(host, gemv::g_timeline, sizeof(gemv::g_timeline));
+}
 extern "C" int vkf_gemv_timing(void *host, int reset) {
     if (reset) {
         static unsigned long long z[512 * 32 * 8];

@@ -282,20 +282,6 @@ __host__ __device__ __forceinline__ int m1_sum_slot(int j) {
     return 2 * t + e;
 }
 
-// Row block end of a column form: each lane holds columns 2t, 2t+1 of rows
-// g, g+8; fold the eight columns into column 0 (lanes t = 0).
-__device__ __forceinline__ void fold_columns(float (&acc)[4]) {
-    float r0 = acc[0] + acc[1], r1 = acc[2] + acc[3];
-    r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
-    r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
-    r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
-    r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
-    acc[0] = r0;
-    acc[1] = 0.f;
-    acc[2] = r1;
-    acc[3] = 0.f;
-}
-
 template <> struct Step<VKF_DEQUANT_Q4_K> : StepK<false> {};
 template <> struct Step<VKF_DEQUANT_Q5_K> : StepK<true> {};
 

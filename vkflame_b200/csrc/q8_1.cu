@@ -41,27 +41,47 @@ __global__ void __launch_bounds__(256) quantize_q8_1_kernel(const float *__restr
     }
 }
 
-// Q8_1 (M rows of K/32 blocks, row stride ldb blocks) -> fp16 M x K (row stride ldo).
+// Q8_1 (M rows of K/32 blocks, row stride ldb blocks) -> fp16 M x K (row stride
+// ldo).  Four threads per block, eight values each: two 4-byte loads of
+// codes (blocks are 36 bytes, so their codes are 4-byte aligned), one 16-byte
+// store.  Grid: (blocks of a row / 64, M).
 __global__ void __launch_bounds__(256) q8_1_to_f16_kernel(const uint8_t *__restrict__ src, __half *__restrict__ dst,
                                                           int M, int K, int64_t ldb, int64_t ldo) {
-    const int lane = threadIdx.x & 31;
-    const int64_t blk = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     const int nbr = K / 32;
-    if (blk >= (int64_t)M * nbr) return;
-    const int64_t m = blk / nbr, b = blk % nbr;
-    const uint8_t *p = src + (m * ldb + b) * 36;
+    const int i = blockIdx.x * 256 + threadIdx.x;  // (block, quarter) within the row
+    const int b = i >> 2, qtr = i & 3;
+    if (b >= nbr) return;
+    const int m = blockIdx.y;
+    const uint8_t *p = src + ((int64_t)m * ldb + b) * 36;
     const float d = __half2float(*reinterpret_cast<const __half *>(p));
-    const int8_t q = reinterpret_cast<const int8_t *>(p + 4)[lane];
-    dst[m * ldo + b * 32 + lane] = __float2half_rn(__fmul_rn(d, (float)q));
+    const uint32_t w0 = *reinterpret_cast<const uint32_t *>(p + 4 + 8 * qtr);
+    const uint32_t w1 = *reinterpret_cast<const uint32_t *>(p + 8 + 8 * qtr);
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t w = k < 2 ? w0 : w1;
+        const int sh = 16 * (k & 1);
+        const float lo = __fmul_rn(d, (float)(int8_t)(w >> sh)), hi = __fmul_rn(d, (float)(int8_t)(w >> (sh + 8)));
+        const __half2 h = __floats2half2_rn(lo, hi);
+        o[k] = *reinterpret_cast<const uint32_t *>(&h);
+    }
+    __half *q = dst + (int64_t)m * ldo + b * 32 + 8 * qtr;
+    if (((uintptr_t)q & 15) == 0) {
+        *reinterpret_cast<uint4 *>(q) = make_uint4(o[0], o[1], o[2], o[3]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) reinterpret_cast<__half2 *>(q)[k] = *reinterpret_cast<const __half2 *>(&o[k]);
+    }
 }
 
 }  // namespace
 
 int q8_1_to_f16(const void *src, void *dst, int M, int K, int64_t ldb, int64_t ldo, cudaStream_t stream) {
-    int64_t blocks = (int64_t)M * (K / 32);
-    if (blocks == 0) return VKF_OK;
-    q8_1_to_f16_kernel<<<(unsigned)((blocks + 7) / 8), 256, 0, stream>>>((const uint8_t *)src, (__half *)dst, M, K,
-                                                                            ldb, ldo);
+    const int nbr = K / 32;
+    if (M == 0 || nbr == 0) return VKF_OK;
+    if (M > 65535) return VKF_ERR_UNSUPPORTED;
+    const dim3 grid((unsigned)((nbr * 4 + 255) / 256), (unsigned)M);
+    q8_1_to_f16_kernel<<<grid, 256, 0, stream>>>((const uint8_t *)src, (__half *)dst, M, K, ldb, ldo);
     return check_launch();
 }
 
