@@ -144,3 +144,54 @@ def test_quant_linear_prefill_q8_1(rt):
     xdq = po.dequant(S.Q8_1, xq_h, M * K // 32).reshape(M, K).astype(np.float64)
     wf = po.dequant(S.Q8_0, w, N * K // 32).reshape(N, K).astype(np.float64)
     assert G.normwise_err(y, xdq @ wf.T) < 2e-3
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("q,M,N,K,f16,ldy", [
+    (S.Q4_K, 300, 200, 2048, True, 256),    # two activation tiles of 256 (second ragged), ragged weight tile
+    (S.Q8_0, 9, 130, 512, False, 130),      # smallest prefill M, one-row second weight tile
+    (S.Q5_K, 64, 256, 5120, False, 264),    # 14B K, padded output rows
+    (S.Q4_0, 129, 384, 4096, True, 384),    # 129 -> activation tiles of 256
+    (S.Q4_K, 96, 1000, 1280, True, 1000),   # 128-wide activation tile, odd N
+])
+def test_quant_linear_prefill_fused_shapes(rt, q, M, N, K, f16, ldy):
+    """Fused-dequant tcgen05 prefill (packed W bytes -> fp16 tiles in shared
+    memory): ragged M and N, fp16 and fp32 outputs, output stride > N; the
+    bytes between N and ldy must stay untouched."""
+    w = S.quant_matrix(q, N, K, seed=50 + q + M)
+    x = S.normal_f16((M, K), seed=M + 1)
+    wd, xd = G.dev(w), G.dev(x)
+    es = 2 if f16 else 4
+    yd = G.empty(M * ldy * es)
+    rt.quant_linear(wd.data_ptr(), q, xd.data_ptr(), rt.X_F16, yd.data_ptr(), rt.Y_F16 if f16 else rt.Y_F32,
+                    M, N, K, K, ldy)
+    yfull = G.host(yd, np.float16 if f16 else np.float32, (M, ldy))
+    wf = po.dequant(q, w, N * K // S.BLOCK_VALUES[q]).reshape(N, K).astype(np.float64)
+    ref = x.astype(np.float64) @ wf.T
+    assert G.normwise_err(yfull[:, :N].astype(np.float64), ref) < G.REL_TOL
+    if ldy > N:
+        pad = G.host(yd, np.uint8, (M, ldy * es))[:, N * es:]
+        assert (pad == 0xFF).all()
+    rt.check_kernel_errors()
+
+
+@pytest.mark.gpu
+def test_quant_linear_prefill_config4_size(rt):
+    """Config 4 at full size (M=512, K=5120, N=13824, Q8_0 x Q8_1): sampled
+    output rows against the fp64 product of the dequantised operands."""
+    M, N, K = 512, 13824, 5120
+    w = S.quant_matrix(S.Q8_0, N, K, seed=77)
+    xf = S.normal_f32((M, K), seed=78)
+    xd, wd = G.dev(xf), G.dev(w)
+    xq = G.empty(M * K // 32 * 36)
+    rt.quantize_q8_1(xd.data_ptr(), xq.data_ptr(), M, K, K)
+    yd = G.empty(M * N * 4)
+    rt.quant_linear(wd.data_ptr(), S.Q8_0, xq.data_ptr(), rt.X_Q8_1, yd.data_ptr(), rt.Y_F32, M, N, K, K // 32, N)
+    y = G.host(yd, np.float32, (M, N))
+    rows = np.array([0, 1, 127, 128, 255, 256, 300, 511])
+    xq_h = G.host(xq, np.uint8).reshape(M, K // 32 * 36)
+    xdq = po.dequant(S.Q8_1, np.ascontiguousarray(xq_h[rows]).ravel(), len(rows) * K // 32).reshape(len(rows), K)
+    wf = po.dequant(S.Q8_0, w, N * K // 32).reshape(N, K).astype(np.float64)
+    ref = xdq.astype(np.float64) @ wf.T
+    assert G.normwise_err(y[rows], ref) < G.REL_TOL
+    rt.check_kernel_errors()

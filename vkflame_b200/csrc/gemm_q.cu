@@ -1,0 +1,734 @@
+// gemm_q.cu — prefill GEMM (M > 8) of ggml-quantised weights with the
+// dequant fused into shared memory, on tcgen05 tensor cores.
+//
+//   Y[m, n] = sum_k X[m, k] * dequant(W)[n, k]      X fp16 [M x K], W ggml rows
+//
+// Replaces the reference's quantised mul_mat chain (shim/hip_runtime_shim.cpp:
+// 1129-1166: dequant W to an fp32 buffer, dequant X, then a K-serial GEMM)
+// and this library's own earlier widen-then-GEMM form: W is read from HBM
+// once, as packed blocks, and never exists in memory as fp16.
+//
+// Roles are swapped against the plain GEMM: the weight tile is the MMA's A
+// operand (128 weight rows = the 128 TMEM lanes) and the activations the B
+// operand (NB x BX rows of X = TMEM columns, up to 512), so a weight tile is
+// dequantised once per up to 512 activation rows and the accumulator's lanes
+// are output columns.
+//
+// Work split (stream-K): the flattened (tile, 256-value K stage) space is cut
+// into one equal contiguous range per CTA, so every SM does the same number
+// of MMAs whatever the tile count.  A CTA's range is [tail of a tile][whole
+// tiles][head of a tile]: whole tiles store Y; a tile's later parts (tails,
+// or a middle when a range lies inside one tile) publish fp32 partials to
+// scratch at the START of their CTAs' runs; the tile's head is processed at
+// the END of its CTA's run, so that CTA finds the partials ready (a bounded
+// wait guards it), adds them in CTA order (deterministic) and stores Y.
+//
+// Warps:
+//   0        TMA producer of the X tiles (fp16, 128-byte swizzle, K-major),
+//            one 64-value K-block per stage;
+//   1        allocates the TMEM accumulator (double-buffered when 2 x NB x BX
+//            columns fit); one thread issues tcgen05.mma kind::f16;
+//   2..5     epilogue: tcgen05.ld, partial publish / fixup, Y stores;
+//   6        TMA producer of the packed weight bytes: ONE 2-D tensor copy
+//            per 128 rows x 256 values (a map over the ggml buffer with
+//            8-byte elements; no per-row operations);
+//   7..7+CV  converters: decode the packed bytes of a K-block into fp16 and
+//            store them in the 128-byte-swizzled K-major layout tcgen05
+//            reads (the layout a SWIZZLE_128B tensor copy would write), then
+//            fence the generic-proxy stores for the async proxy and arrive.
+// Each fp16 weight is the value the reference's dequant shader computes,
+// rounded once to fp16 (the same rounding as the widen path it replaces).
+// The MMA stage's barrier completes when the X copy has landed AND all
+// converter warps have arrived.
+
+#include "tc_common.cuh"
+#include "rt_internal.h"
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstring>
+#include <climits>
+#include <type_traits>
+
+namespace vkf {
+namespace qgemm {
+
+constexpr int BW = 128;   // weight rows per tile (MMA M, TMEM lanes)
+constexpr int KV = 64;    // K values per MMA stage (128 bytes of fp16 per row)
+constexpr int RV = 256;   // K values per packed-weight stage (the work unit)
+constexpr int CV = 8;     // converter warps
+constexpr int W_RAW = 6, W_CONV = 7;
+constexpr int NT = 32 * (W_CONV + CV);
+constexpr int A_BYTES = BW * 128;
+constexpr int SMEM_CAP = 232448;
+constexpr int EPI_BUF = 4096;  // one Y staging buffer: 16 rows fp16 / 8 rows fp32 of 128 columns
+
+// Packed bytes of one row's 256 values.
+template <int QT>
+struct Packed;
+template <> struct Packed<VKF_DEQUANT_Q4_0> { static constexpr int RB = 8 * 18; };
+template <> struct Packed<VKF_DEQUANT_Q8_0> { static constexpr int RB = 8 * 34; };
+template <> struct Packed<VKF_DEQUANT_Q4_K> { static constexpr int RB = 144; };
+template <> struct Packed<VKF_DEQUANT_Q5_K> { static constexpr int RB = 176; };
+
+#ifdef VKF_QGEMM_TIMING
+// Cycle accumulators per CTA: [0] converter raw wait, [1] converter empty
+// wait, [2] converter work, [3] MMA full wait, [4] MMA thread done (since
+// start), [5] X producer empty wait, [6] epilogue busy, [7] total.
+__device__ unsigned long long g_qt[512][8];
+#define QT_T0 const long long _t0 = clock64()
+#define QT_ACC(i) if (lane == 0) atomicAdd(&g_qt[blockIdx.x][i], (unsigned long long)(clock64() - _t0))
+#else
+#define QT_T0
+#define QT_ACC(i)
+#endif
+
+struct Params {
+    int M, N, K;
+    void *Y;
+    int64_t ldy;
+    int y_f16;
+    int y_tma;        // Y written by 2-D tensor stores (16-byte aligned rows)
+    int units;        // tiles x (K / 256)
+    float *ws;        // per CTA: [NB*BX/4][128][4] fp32 partials (4-column groups)
+    int *flags;       // [grid] partial published (reset by the consumer)
+    unsigned *err;
+};
+
+// Segment walk shared by every role: CTA c owns units [u0, u1); a segment is
+// the part of one tile inside that range.
+struct Seg {
+    int tile, kr0, kr1;
+};
+__device__ __forceinline__ int unit_begin(int c, int units) { return (int)((int64_t)c * units / gridDim.x); }
+__device__ __forceinline__ int cta_of_unit(int u, int units) {
+    return (int)(((int64_t)(u + 1) * gridDim.x - 1) / units);
+}
+
+__device__ __forceinline__ uint32_t lds16(const uint8_t *p) { return *reinterpret_cast<const uint16_t *>(p); }
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+// get_scale_min_k4 (dequant_q4_k.glsl:16-24) for sub-blocks j and j+1
+// (j even) from the 12 packed scale bytes.
+__device__ __forceinline__ void scale_min_k4(int j, const uint8_t *s, int &sc, int &mn) {
+    if (j < 4) {
+        sc = s[j] & 63;
+        mn = s[j + 4] & 63;
+    } else {
+        sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+        mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+// One converter lane's share of a 64-value K-block of row `rp` (the row's
+// 256-value packed stage): 16 values as two 16-byte chunks (chunk indices
+// within the K-block in ca, cb).  cp = lane & 3 selects which 16.
+template <int QT>
+__device__ __forceinline__ void convert16(const uint8_t *rp, int kk, int cp, uint4 &oa, uint4 &ob, int &ca,
+                                          int &cb) {
+    uint32_t o[8];
+    if constexpr (QT == VKF_DEQUANT_Q8_0) {  // dequant_q8_0.glsl: d * q; chunks 2cp, 2cp+1
+        const uint8_t *bp = rp + 34 * (2 * kk + (cp >> 1));
+        const __half2 d2 = __half2half2(*reinterpret_cast<const __half *>(bp));
+        // 16 code bytes at a 2-byte aligned address: five aligned words, shifted.
+        const uint8_t *cpt = bp + 2 + 16 * (cp & 1);
+        const uint32_t *wp = reinterpret_cast<const uint32_t *>((uintptr_t)cpt & ~(uintptr_t)3);
+        const uint32_t sh = ((uintptr_t)cpt & 3) * 8;
+        uint32_t w[5];
+#pragma unroll
+        for (int i = 0; i < 5; ++i) w[i] = wp[i];
+        const __half2 off = __float2half2_rn(1152.0f);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            // fp16 1024 + (q + 128), exact; minus 1152 = q, exact; one rounding in the product.
+            const uint32_t x = __funnelshift_r(w[i], w[i + 1], sh) ^ 0x80808080u;
+            o[2 * i] = h2u(__hmul2(__hsub2(u2h(__byte_perm(x, 0x64646464u, 0x4140)), off), d2));
+            o[2 * i + 1] = h2u(__hmul2(__hsub2(u2h(__byte_perm(x, 0x64646464u, 0x4342)), off), d2));
+        }
+        ca = 2 * cp;
+        cb = 2 * cp + 1;
+    } else if constexpr (QT == VKF_DEQUANT_Q4_0) {  // dequant_q4_0.glsl: d * (q - 8)
+        // chunk ca = low nibbles of 8 code bytes, cb = ca + 2 their high nibbles
+        const uint8_t *bp = rp + 18 * (2 * kk + (cp >> 1));
+        const __half2 d2 = __half2half2(*reinterpret_cast<const __half *>(bp));
+        const uint8_t *cpt = bp + 2 + 8 * (cp & 1);
+        const uint32_t w0 = lds16(cpt) | (lds16(cpt + 2) << 16), w1 = lds16(cpt + 4) | (lds16(cpt + 6) << 16);
+        const uint32_t ws[4] = {w0, w1, w0 >> 4, w1 >> 4};
+        const __half2 off = __float2half2_rn(1032.0f);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t p0 = __byte_perm(ws[i], 0, 0x4140), p1 = __byte_perm(ws[i], 0, 0x4342);
+            o[2 * i] = h2u(__hmul2(__hsub2(u2h((p0 & 0x000F000Fu) | 0x64006400u), off), d2));
+            o[2 * i + 1] = h2u(__hmul2(__hsub2(u2h((p1 & 0x000F000Fu) | 0x64006400u), off), d2));
+        }
+        ca = (cp & 1) + 4 * (cp >> 1);
+        cb = ca + 2;
+    } else {  // Q4_K / Q5_K, dequant_q4_k.glsl:35-57, dequant_q5_k.glsl:37-74: d*sc*q - dmin*m
+        // chunk cp = low nibbles (sub-block 2kk), cp + 4 = high nibbles (2kk + 1)
+        constexpr bool Q5 = QT == VKF_DEQUANT_Q5_K;
+        const int j = 2 * kk;
+        const float d = __half2float(*reinterpret_cast<const __half *>(rp));
+        const float dmin = __half2float(*reinterpret_cast<const __half *>(rp + 2));
+        int sc0, mn0, sc1, mn1;
+        scale_min_k4(j, rp + 4, sc0, mn0);
+        scale_min_k4(j + 1, rp + 4, sc1, mn1);
+        const float dd[2] = {d * (float)sc0, d * (float)sc1}, mm[2] = {dmin * (float)mn0, dmin * (float)mn1};
+        const uint2 q = *reinterpret_cast<const uint2 *>(rp + (Q5 ? 48 : 16) + 32 * kk + 8 * cp);
+        uint2 h = make_uint2(0u, 0u);
+        if constexpr (Q5) h = *reinterpret_cast<const uint2 *>(rp + 16 + 8 * cp);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const uint32_t qw[2] = {(q.x >> (4 * half)) & 0x0F0F0F0Fu, (q.y >> (4 * half)) & 0x0F0F0F0Fu};
+            uint32_t hw[2] = {0u, 0u};
+            if constexpr (Q5) {
+                hw[0] = ((h.x >> (j + half)) & 0x01010101u) << 4;
+                hw[1] = ((h.y >> (j + half)) & 0x01010101u) << 4;
+            }
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const uint32_t c = qw[i] | hw[i];
+                float f[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    // 2^23 + code, exact; dd*q is exact in fp32, so the fma
+                    // equals the shader's multiply-then-subtract.
+                    const float qf = __uint_as_float(0x4B000000u | ((c >> (8 * e)) & 0xFFu)) - 8388608.0f;
+                    f[e] = fmaf(dd[half], qf, -mm[half]);
+                }
+                o[4 * half + 2 * i] = h2u(__floats2half2_rn(f[0], f[1]));
+                o[4 * half + 2 * i + 1] = h2u(__floats2half2_rn(f[2], f[3]));
+            }
+        }
+        ca = cp;
+        cb = cp + 4;
+    }
+    oa = make_uint4(o[0], o[1], o[2], o[3]);
+    ob = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+// Row (within a group of 8) served by lane group g = lane >> 2, ordered so
+// that each 8-lane store phase writes 8 distinct 16-byte bank groups of the
+// swizzled tile: chunk sets {2cp} (Q8_0) pair rows r, r^1; {cp} (K-quants)
+// rows r, r^4; {(cp&1) + 4(cp>>1)} (Q4_0) rows r, r^2.
+template <int QT>
+__device__ __forceinline__ int row_of_group(int g) {
+    const int lo = g & 1, hi = g >> 1;  // lo: the row pair inside a phase
+    if constexpr (QT == VKF_DEQUANT_Q8_0) return 2 * hi + lo;
+    else if constexpr (QT == VKF_DEQUANT_Q4_0) return (hi & 1) + 4 * (hi >> 1) + 2 * lo;
+    else return hi + 4 * lo;
+}
+
+__device__ __forceinline__ bool wait_flag(const int *f, unsigned *err) {
+    for (uint32_t i = 0; i < (1u << 24); ++i) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        if (v) return true;
+        __nanosleep(64);
+    }
+    if (err) atomicOr(err, VKF_KERR_WAIT_TIMEOUT);
+    return false;
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// AND of v over the four epilogue warps (keeps their barrier sequences equal).
+__device__ __forceinline__ bool epi_all(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, 1, 128, q;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
+
+template <int QT, int BX, int NB, int NS, int RS>
+__global__ void __launch_bounds__(NT, 1)
+    qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                 const __grid_constant__ CUtensorMap tmY, const __grid_constant__ Params p) {
+    constexpr int RB = Packed<QT>::RB;
+    constexpr int NC = NB * BX;  // accumulator columns per tile
+    constexpr int B_BYTES = NC * 128, STAGE = A_BYTES + B_BYTES;
+    constexpr int RAW_BYTES = (BW * RB + 127) / 128 * 128;
+    constexpr int NBUF = 2 * NC <= 512 ? 2 : 1;
+    constexpr uint32_t IDESC = tc::instr_desc(tc::KIND_F16, BW, BX);
+    constexpr uint32_t TCOLS = NBUF * NC <= 32 ? 32 : NBUF * NC <= 64 ? 64 : NBUF * NC <= 128 ? 128
+                             : NBUF * NC <= 256 ? 256 : 512;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *raw = smem + NS * STAGE;
+    uint8_t *ystage = raw + RS * RAW_BYTES;  // 2 x EPI_BUF
+    uint64_t *ab_full = reinterpret_cast<uint64_t *>(ystage + 2 * EPI_BUF);
+    uint64_t *ab_empty = ab_full + NS;
+    uint64_t *raw_full = ab_empty + NS;
+    uint64_t *raw_empty = raw_full + RS;
+    uint64_t *acc_full = raw_empty + RS;
+    uint64_t *acc_empty = acc_full + 2;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    int *sflag = reinterpret_cast<int *>(tslot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int x_tiles = (p.M + NC - 1) / NC;
+    const int KR = p.K / RV;
+    const int u_begin = unit_begin(blockIdx.x, p.units), u_end = unit_begin(blockIdx.x + 1, p.units);
+    auto seg_at = [&](int u) {
+        Seg sg;
+        sg.tile = u / KR;
+        sg.kr0 = u - sg.tile * KR;
+        sg.kr1 = min(KR, sg.kr0 + (u_end - u));
+        return sg;
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&ab_full[s], CV + 1);
+            mbar_init(&ab_empty[s], 1);
+        }
+        for (int s = 0; s < RS; ++s) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], CV);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) tc::tmem_alloc(tslot, TCOLS);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem0 = *tslot;
+#ifdef VKF_QGEMM_TIMING
+    const long long t_start = clock64();
+#endif
+
+    if (warp == 0) {
+        // ---- X tiles: NB boxes of BX rows per K-block ----
+        if (lane == 0) {
+            int g = 0;
+            bool ok = true;
+            for (int u = u_begin; u < u_end && ok;) {
+                const Seg sg = seg_at(u);
+                u += sg.kr1 - sg.kr0;
+                const int m0 = (sg.tile % x_tiles) * NC;
+                for (int kb = sg.kr0 * (RV / KV); kb < sg.kr1 * (RV / KV); ++kb, ++g) {
+                    const int s = g % NS;
+                    {
+                        QT_T0;
+                        if (g >= NS && !(ok = mbar_wait(&ab_empty[s], ((g / NS) & 1) ^ 1, p.err))) break;
+                        QT_ACC(5);
+                    }
+                    mbar_arrive_expect_tx(&ab_full[s], B_BYTES);
+#pragma unroll
+                    for (int h = 0; h < NB; ++h)
+                        tc::tma_load_2d(smem + s * STAGE + A_BYTES + h * BX * 128, &tmX, kb * KV, m0 + h * BX,
+                                        &ab_full[s]);
+                }
+            }
+        }
+    } else if (warp == W_RAW) {
+        // ---- packed weight bytes: one tensor copy per 128 rows x 256 values ----
+        if (lane == 0) {
+            int g = 0;
+            bool ok = true;
+            for (int u = u_begin; u < u_end && ok;) {
+                const Seg sg = seg_at(u);
+                u += sg.kr1 - sg.kr0;
+                const int n0 = (sg.tile / x_tiles) * BW;
+                for (int kr = sg.kr0; kr < sg.kr1; ++kr, ++g) {
+                    const int s = g % RS;
+                    if (g >= RS && !(ok = mbar_wait(&raw_empty[s], ((g / RS) & 1) ^ 1, p.err))) break;
+                    mbar_arrive_expect_tx(&raw_full[s], BW * RB);
+                    tc::tma_load_2d(raw + s * RAW_BYTES, &tmW, kr * (RB / 8), n0, &raw_full[s]);
+                }
+            }
+        }
+    } else if (warp >= W_CONV) {
+        // ---- converters: warp cw owns rows 16 cw .. 16 cw + 15 ----
+        const int cw = warp - W_CONV;
+        const int cp = lane & 3;
+        int rows[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) rows[i] = 16 * cw + 8 * i + row_of_group<QT>(lane >> 2);
+        int g = 0, gr = 0;
+        bool ok = true;
+        for (int u = u_begin; u < u_end && ok; ++u, ++gr) {
+            const int rs = gr % RS;
+            {
+                QT_T0;
+                if (!(ok = mbar_wait(&raw_full[rs], (gr / RS) & 1, p.err))) break;
+                QT_ACC(0);
+            }
+            const uint8_t *rt = raw + rs * RAW_BYTES;
+#pragma unroll 1
+            for (int kk = 0; kk < RV / KV; ++kk, ++g) {
+                const int s = g % NS;
+                {
+                    QT_T0;
+                    if (g >= NS && !(ok = mbar_wait(&ab_empty[s], ((g / NS) & 1) ^ 1, p.err))) break;
+                    QT_ACC(1);
+                }
+                QT_T0;
+                uint8_t *at = smem + s * STAGE;
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const int r = rows[i];
+#ifndef VKF_QGEMM_NOCONV
+                    uint4 va, vb;
+                    int ca, cb;
+                    convert16<QT>(rt + r * RB, kk, cp, va, vb, ca, cb);
+                    uint8_t *rowp = at + (r >> 3) * 1024 + (r & 7) * 128;
+#ifdef VKF_QGEMM_NOSTS
+                    if ((va.x ^ vb.y) == 0x12345678u)  // keep the conversion live
+#endif
+                    {
+                        *reinterpret_cast<uint4 *>(rowp + ((ca ^ (r & 7)) << 4)) = va;
+                        *reinterpret_cast<uint4 *>(rowp + ((cb ^ (r & 7)) << 4)) = vb;
+                    }
+#endif
+                }
+                // generic-proxy stores -> visible to the tensor core's async proxy
+#ifndef VKF_QGEMM_NOFENCE
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+#endif
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ab_full[s]);
+                QT_ACC(2);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[rs]);
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer ----
+        if (lane == 0) {
+            int g = 0, it = 0;
+            bool ok = true;
+            for (int u = u_begin; u < u_end && ok; ++it) {
+                const Seg sg = seg_at(u);
+                u += sg.kr1 - sg.kr0;
+                const int b = NBUF == 2 ? (it & 1) : 0;
+                const int use = NBUF == 2 ? (it >> 1) : it;  // earlier uses of buffer b
+                if (use >= 1 && !(ok = mbar_wait(&acc_empty[b], (use - 1) & 1, p.err))) break;
+                tc::fence_after_sync();
+                const uint32_t tmem = tmem0 + b * NC;
+                const int kb0 = sg.kr0 * (RV / KV), kb1 = sg.kr1 * (RV / KV);
+                for (int kb = kb0; kb < kb1; ++kb, ++g) {
+                    const int s = g % NS;
+                    {
+                        QT_T0;
+                        if (!(ok = mbar_wait(&ab_full[s], (g / NS) & 1, p.err))) break;
+                        QT_ACC(3);
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t sa = smem_addr(smem + s * STAGE), sb = sa + A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+                        for (int h = 0; h < NB; ++h)
+                            tc::mma<tc::KIND_F16>(tmem + h * BX, tc::smem_desc_sw128(sa + kk * 32),
+                                                  tc::smem_desc_sw128(sb + h * BX * 128 + kk * 32), IDESC,
+                                                  (kb > kb0 || kk) ? 1u : 0u);
+                    tc::commit(&ab_empty[s]);
+                }
+                tc::commit(&acc_full[b]);
+            }
+#ifdef VKF_QGEMM_TIMING
+            atomicAdd(&g_qt[blockIdx.x][4], (unsigned long long)(clock64() - t_start));
+#endif
+        }
+    } else {
+        // ---- epilogue (warps 2..5): TMEM lane = weight row = output column ----
+        const int q = warp & 3;
+        const int tid = threadIdx.x - 64;  // 0..127 over the four epilogue warps
+        int it = 0;
+        uint32_t ybuf = 0;  // Y staging buffers used so far
+        for (int u = u_begin; u < u_end; ++it) {
+            const Seg sg = seg_at(u);
+            u += sg.kr1 - sg.kr0;
+            const int b = NBUF == 2 ? (it & 1) : 0;
+            const int use = NBUF == 2 ? (it >> 1) : it;
+            const int m0 = (sg.tile % x_tiles) * NC, nl = 32 * q + lane, n = (sg.tile / x_tiles) * BW + nl;
+            bool ok = epi_all(mbar_wait(&acc_full[b], use & 1, p.err));
+#ifdef VKF_QGEMM_TIMING
+            const long long te0 = clock64();
+#endif
+            tc::fence_after_sync();
+            const uint32_t tmem = tmem0 + b * NC + ((uint32_t)(32 * q) << 16);
+            const bool whole = sg.kr0 == 0 && sg.kr1 == KR;
+            if (sg.kr0 > 0) {
+                // a later part of the tile: publish the partial for the head's
+                // CTA as float4 groups [chunk][4-column group][lane][4], so a
+                // warp's store of one group is 512 contiguous bytes
+                float4 *wsp = reinterpret_cast<float4 *>(p.ws + (size_t)blockIdx.x * NC * BW) + nl;
+#pragma unroll 1
+                for (int cc = 0; cc < NC / 32; ++cc) {
+                    uint32_t r[32];
+                    tc::tmem_ld32(tmem + 32 * cc, r);
+#pragma unroll
+                    for (int j4 = 0; j4 < 8; ++j4)
+                        __stcg(wsp + (size_t)(cc * 8 + j4) * BW,
+                               make_float4(__uint_as_float(r[4 * j4]), __uint_as_float(r[4 * j4 + 1]),
+                                           __uint_as_float(r[4 * j4 + 2]), __uint_as_float(r[4 * j4 + 3])));
+                }
+                tc::fence_before_sync();
+                epi_bar();
+                if (tid == 0) {
+                    __threadfence();
+                    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p.flags + blockIdx.x), "r"(1) : "memory");
+                }
+            } else {
+                // whole tile, or the head: add the later parts (CTAs c+1 .. c_last) first
+                int c_last = blockIdx.x;
+                if (!whole) {
+                    c_last = cta_of_unit(sg.tile * KR + KR - 1, p.units);
+                    if (tid == 0) {
+                        bool fine = ok;
+                        for (int c = blockIdx.x + 1; c <= c_last && fine; ++c) fine = wait_flag(p.flags + c, p.err);
+                        *sflag = fine;
+                    }
+                    epi_bar();
+                    ok = ok && *sflag;
+                }
+#pragma unroll 1
+                for (int cc = 0; cc < NC / 32; ++cc) {
+                    // partial loads first (independent of TMEM): their L2
+                    // latency overlaps the accumulator read
+                    float v[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = 0.f;
+                    if (ok)
+                        for (int c = blockIdx.x + 1; c <= c_last; ++c) {
+                            const float4 *wsp = reinterpret_cast<const float4 *>(p.ws + (size_t)c * NC * BW) +
+                                                (size_t)(cc * 8) * BW + nl;
+                            float4 t[8];
+#pragma unroll
+                            for (int j4 = 0; j4 < 8; ++j4) t[j4] = __ldcg(wsp + (size_t)j4 * BW);
+#pragma unroll
+                            for (int j4 = 0; j4 < 8; ++j4) {
+                                v[4 * j4] += t[j4].x;
+                                v[4 * j4 + 1] += t[j4].y;
+                                v[4 * j4 + 2] += t[j4].z;
+                                v[4 * j4 + 3] += t[j4].w;
+                            }
+                        }
+                    uint32_t r[32];
+                    tc::tmem_ld32(tmem + 32 * cc, r);
+                    const int mc = m0 + 32 * cc;
+                    // own part first, then the later parts in CTA order
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + v[j];
+                    if (p.y_tma) {
+                        // Stage SR rows x 128 columns in shared memory and
+                        // write them with one tensor store (out-of-range rows
+                        // and columns are clipped by the store).  Every
+                        // epilogue thread takes part in every barrier.
+                        if (mc >= p.M) continue;  // uniform across the epilogue warps
+                        auto stage_store = [&](auto sr_c) {
+                            constexpr int SR = decltype(sr_c)::value;
+#pragma unroll
+                            for (int sub = 0; sub < 32; sub += SR, ++ybuf) {
+                                uint8_t *buf = ystage + (ybuf & 1) * EPI_BUF;
+                                if (tid == 0) tc::bulk_wait_read<1>();
+                                epi_bar();
+#pragma unroll
+                                for (int i = 0; i < SR; ++i) {
+                                    if constexpr (SR == 16)
+                                        reinterpret_cast<__half *>(buf)[i * BW + nl] = __float2half_rn(v[sub + i]);
+                                    else
+                                        reinterpret_cast<float *>(buf)[i * BW + nl] = v[sub + i];
+                                }
+                                tc::fence_proxy_async();
+                                epi_bar();
+                                if (tid == 0 && ok) {
+                                    tc::tma_store_2d(&tmY, buf, n - nl, mc + sub);
+                                    tc::bulk_commit();
+                                }
+                            }
+                        };
+                        if (p.y_f16) stage_store(std::integral_constant<int, 16>{});
+                        else stage_store(std::integral_constant<int, 8>{});
+                        continue;
+                    }
+                    if (!ok || n >= p.N || mc >= p.M) continue;
+                    const int nm = min(32, p.M - mc);
+#ifdef VKF_QGEMM_NOY
+                    if (v[0] == 1234.5f && v[31] == -1.f)
+#endif
+                    if (p.y_f16) {
+                        __half *yp = reinterpret_cast<__half *>(p.Y) + (int64_t)mc * p.ldy + n;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < nm) yp[(int64_t)j * p.ldy] = __float2half_rn(v[j]);
+                    } else {
+                        float *yp = reinterpret_cast<float *>(p.Y) + (int64_t)mc * p.ldy + n;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < nm) yp[(int64_t)j * p.ldy] = v[j];
+                    }
+                }
+                // flags consumed: leave them zeroed for the next launch
+                if (!whole && tid == 0)
+                    for (int c = blockIdx.x + 1; c <= c_last; ++c) p.flags[c] = 0;
+                tc::fence_before_sync();
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
+#ifdef VKF_QGEMM_TIMING
+            if (q == 2 && lane == 0) atomicAdd(&g_qt[blockIdx.x][6], (unsigned long long)(clock64() - te0));
+#endif
+            if (!ok) break;
+        }
+        if (tid == 0) tc::bulk_wait_all();  // Y tensor stores performed before exit
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+#ifdef VKF_QGEMM_TIMING
+    if (threadIdx.x == 0) atomicAdd(&g_qt[blockIdx.x][7], (unsigned long long)(clock64() - t_start));
+#endif
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_free(tmem0, TCOLS);
+    }
+}
+
+template <int QT, int BX, int NB>
+struct Cfg {
+    static constexpr int RB = Packed<QT>::RB;
+    static constexpr int RAW_BYTES = (BW * RB + 127) / 128 * 128;
+    static constexpr int STAGE = A_BYTES + NB * BX * 128;
+    static constexpr int FIXED = 1024 + 256 + 2 * EPI_BUF;
+    // Deepest A/B ring (<= 4) that still leaves two packed stages, then as
+    // many packed stages (<= 6) as fit.
+    static constexpr int NS = (SMEM_CAP - FIXED - 2 * RAW_BYTES) / STAGE >= 4 ? 4
+                              : (SMEM_CAP - FIXED - 2 * RAW_BYTES) / STAGE;
+    static constexpr int RS0 = (SMEM_CAP - FIXED - NS * STAGE) / RAW_BYTES;
+    static constexpr int RS = RS0 > 6 ? 6 : RS0;
+    static constexpr size_t SMEM = (size_t)NS * STAGE + (size_t)RS * RAW_BYTES + FIXED;
+    static constexpr bool FITS = NS >= 2 && RS >= 2;
+};
+
+// Columns per tile (NB x BX) for M activation rows; mirrors launch_q.
+template <int QT>
+static int tile_cols(int M) {
+    if constexpr (Cfg<QT, 256, 2>::FITS) {
+        if (M > 256) return 512;
+    }
+    return M > 128 ? 256 : M > 64 ? 128 : M > 32 ? 64 : 32;
+}
+
+static int grid_for(int units) {
+    DeviceState *ds = device_state();
+    return std::max(1, std::min(units, ds ? ds->sm_count : 148));
+}
+
+template <int QT, int BX, int NB>
+static int launch(const void *W, const void *X, int64_t ldx, void *Y, int y_f16, int64_t ldy, int M, int N, int K,
+                  float *ws, cudaStream_t stream) {
+    using C = Cfg<QT, BX, NB>;
+    static_assert(C::FITS, "ring does not fit shared memory");
+    constexpr int NC = BX * NB;
+    const int64_t row_bytes = (int64_t)K / RV * C::RB;
+    CUtensorMap tx, tw;
+    if (!make_kmajor_map(&tx, X, 2, M, K, ldx, BX) || !make_byte_matrix_map(&tw, W, N, row_bytes, C::RB, BW))
+        return VKF_ERR_UNSUPPORTED;
+    auto kern = qgemm_kernel<QT, BX, NB, C::NS, C::RS>;
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM) != cudaSuccess)
+            return VKF_ERR_CUDA;
+        attr[dev] = true;
+    }
+    DeviceState *ds = device_state();
+    if (!ds) return VKF_ERR_NO_DEVICE;
+    const int tiles = ((M + NC - 1) / NC) * ((N + BW - 1) / BW);
+    const int units = tiles * (K / RV);
+    const int grid = grid_for(units);
+    int *flags = stream_counters(stream, (size_t)grid);
+    if (!flags) return VKF_ERR_NOMEM;
+    // Y rows 16-byte aligned: tensor stores of 16 (fp16) or 8 (fp32) rows x 128 columns
+    CUtensorMap ty;
+    memset(&ty, 0, sizeof(ty));
+    const int esize = y_f16 ? 2 : 4;
+    const int y_tma = make_rowmajor_map(&ty, Y, esize, M, N, ldy, BW, EPI_BUF / (BW * esize)) ? 1 : 0;
+    Params p{M, N, K, Y, ldy, y_f16, y_tma, units, ws, flags, ds->d_error};
+    kern<<<grid, NT, C::SMEM, stream>>>(tx, tw, ty, p);
+    return check_launch();
+}
+
+// Activation columns per tile: all of M up to 512 (one weight-tile decode per
+// 512 activation rows), in one or two MMAs of up to 256 columns; 256 for
+// Q8_0, whose 34 KB packed stages leave no room for a 512-column ring.
+template <int QT>
+static int launch_q(const void *W, const void *X, int64_t ldx, void *Y, int y_f16, int64_t ldy, int M, int N, int K,
+                    float *ws, cudaStream_t stream) {
+    switch (tile_cols<QT>(M)) {
+    case 512:
+        if constexpr (Cfg<QT, 256, 2>::FITS) return launch<QT, 256, 2>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
+        return VKF_ERR_UNSUPPORTED;
+    case 256: return launch<QT, 256, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
+    case 128: return launch<QT, 128, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
+    case 64: return launch<QT, 64, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
+    default: return launch<QT, 32, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
+    }
+}
+
+template <int QT>
+static size_t ws_bytes_q(int M, int N, int K) {
+    const int nc = tile_cols<QT>(M);
+    const int64_t units = (int64_t)((M + nc - 1) / nc) * ((N + BW - 1) / BW) * (K / RV);
+    return (size_t)grid_for((int)std::min<int64_t>(units, INT32_MAX)) * nc * BW * sizeof(float);
+}
+
+}  // namespace qgemm
+
+// Fused-dequant prefill GEMM; VKF_ERR_UNSUPPORTED when the format or the
+// buffer geometry is not one it serves (the caller then widens W first):
+// Q4_0, Q8_0, Q4_K, Q5_K with K a multiple of 256, W 16-byte aligned; X fp16
+// rows 16-byte aligned.
+bool qgemm_supported(int wtype, const void *W, int K) {
+    return (wtype == VKF_DEQUANT_Q4_0 || wtype == VKF_DEQUANT_Q8_0 || wtype == VKF_DEQUANT_Q4_K ||
+            wtype == VKF_DEQUANT_Q5_K) &&
+           K % qgemm::RV == 0 && ((uintptr_t)W & 15) == 0;
+}
+
+// Scratch the launch needs for the partials of split tiles (bytes).
+size_t qgemm_ws_bytes(int wtype, int M, int N, int K) {
+    switch (wtype) {
+    case VKF_DEQUANT_Q4_0: return qgemm::ws_bytes_q<VKF_DEQUANT_Q4_0>(M, N, K);
+    case VKF_DEQUANT_Q8_0: return qgemm::ws_bytes_q<VKF_DEQUANT_Q8_0>(M, N, K);
+    case VKF_DEQUANT_Q4_K: return qgemm::ws_bytes_q<VKF_DEQUANT_Q4_K>(M, N, K);
+    case VKF_DEQUANT_Q5_K: return qgemm::ws_bytes_q<VKF_DEQUANT_Q5_K>(M, N, K);
+    default: return 0;
+    }
+}
+
+// ws: at least qgemm_ws_bytes(...) of device scratch, 16-byte aligned.
+int qgemm_launch(int wtype, const void *W, const void *X, int64_t ldx, void *Y, int y_f16, int64_t ldy, int M, int N,
+                 int K, float *ws, cudaStream_t stream) {
+    if (!qgemm_supported(wtype, W, K) || ((uintptr_t)X & 15) || (ldx * 2) % 16) return VKF_ERR_UNSUPPORTED;
+    if ((int64_t)((M + 511) / 512) * ((N + 127) / 128) * (K / qgemm::RV) > INT32_MAX / 2) return VKF_ERR_UNSUPPORTED;
+    switch (wtype) {
+    case VKF_DEQUANT_Q4_0: return qgemm::launch_q<VKF_DEQUANT_Q4_0>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
+    case VKF_DEQUANT_Q8_0: return qgemm::launch_q<VKF_DEQUANT_Q8_0>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
+    case VKF_DEQUANT_Q4_K: return qgemm::launch_q<VKF_DEQUANT_Q4_K>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
+    case VKF_DEQUANT_Q5_K: return qgemm::launch_q<VKF_DEQUANT_Q5_K>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
+    default: return VKF_ERR_UNSUPPORTED;
+    }
+}
+
+}  // namespace vkf
+
+#ifdef VKF_QGEMM_TIMING
+extern "C" int vkf_qgemm_timing(void *host, int reset) {
+    if (reset) {
+        static unsigned long long z[512][8];
+        return (int)cudaMemcpyToSymbol(vkf::qgemm::g_qt, z, sizeof(z));
+    }
+    return (int)cudaMemcpyFromSymbol(host, vkf::qgemm::g_qt, sizeof(vkf::qgemm::g_qt));
+}
+#endif

@@ -348,6 +348,45 @@ static bool make_map(CUtensorMap *m, const void *base, int esize, int64_t rows, 
     return r == CUDA_SUCCESS;
 }
 
+}  // namespace gemm
+
+bool make_kmajor_map(CUtensorMap *m, const void *base, int esize, int64_t rows, int64_t cols, int64_t ld,
+                     int box_rows) {
+    return gemm::make_map(m, base, esize, rows, cols, ld, gemm::BKB / esize, box_rows);
+}
+
+bool make_rowmajor_map(CUtensorMap *m, const void *base, int esize, int64_t rows, int64_t cols, int64_t ld,
+                       int box_cols, int box_rows) {
+    auto fn = gemm::encode_fn();
+    if (!fn || ((uintptr_t)base & 15) || (ld * esize) % 16 || (box_cols * esize) % 16 || box_cols > 256 ||
+        box_rows > 256)
+        return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * esize)};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+              const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_byte_matrix_map(CUtensorMap *m, const void *base, int64_t rows, int64_t row_bytes, int box_bytes,
+                          int box_rows) {
+    auto fn = gemm::encode_fn();
+    if (!fn || row_bytes % 16 || box_bytes % 8 || ((uintptr_t)base & 15) || box_bytes / 8 > 256 || box_rows > 256)
+        return false;
+    cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 8), (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)(box_bytes / 8), (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+namespace gemm {
+
 static bool rows16(const void *p, int64_t ld, int esize) {
     return ((uintptr_t)p & 15) == 0 && (ld * esize) % 16 == 0;
 }

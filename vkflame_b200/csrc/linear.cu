@@ -28,6 +28,10 @@ int gemm_tf32_tn(const float *A, int64_t lda, const float *B, int64_t ldb, int M
 int gemm_f16_tn(const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K, float alpha, float beta,
                 const void *C, int64_t ldc, int c_f16, const void *bias, int act, void *Y, int64_t ldy, int y_f16,
                 cudaStream_t stream);
+bool qgemm_supported(int wtype, const void *W, int K);
+size_t qgemm_ws_bytes(int wtype, int M, int N, int K);
+int qgemm_launch(int wtype, const void *W, const void *X, int64_t ldx, void *Y, int y_f16, int64_t ldy, int M, int N,
+                 int K, float *ws, cudaStream_t stream);
 int transpose(const void *src, int64_t lds, void *dst, int64_t ldd, int rows, int cols, int esize,
               cudaStream_t stream);
 
@@ -43,31 +47,48 @@ static int gemv_max_m() {
 
 static size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
 
-// Prefill path: widen W to fp16 (one rounding per weight) and X to fp16
-// rows, then the tcgen05 f16 GEMM with fp32 accumulation.
+// VKFLAME_FUSED_PREFILL=0 routes prefill through widen-then-GEMM (A/B runs).
+static bool fused_prefill_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("VKFLAME_FUSED_PREFILL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// Prefill path.  X reaches the GEMM as fp16 rows at 16-byte aligned
+// addresses (Q8_1 activations widened, misaligned rows staged: M*K*2 bytes,
+// small next to W).  Q4_0 / Q8_0 / Q4_K / Q5_K with K a multiple of 256 take
+// the fused-dequant tcgen05 GEMM (W read once as packed blocks); otherwise W
+// is widened to fp16 (one rounding per weight) and the f16 tcgen05 GEMM runs.
 static int quant_linear_gemm(const void *W, int wtype, const void *X, int xtype, void *Y, int ytype, int M, int N,
                              int K, int64_t ldx, int64_t ldy, cudaStream_t stream) {
-    const size_t wbytes = align256((size_t)N * K * 2), xbytes = align256((size_t)M * K * 2);
-    uint8_t *scr = (uint8_t *)stream_scratch(stream, wbytes + xbytes);
+    if (((size_t)K * 2) % 16) return VKF_ERR_UNSUPPORTED;
+    const bool fused = fused_prefill_enabled() && qgemm_supported(wtype, W, K);
+    // Staged X, then the widened W (widen path) or the split-tile partials
+    // (fused path): one request, since growing the arena drops its contents.
+    const size_t xbytes = align256((size_t)M * K * 2);
+    const size_t wbytes = fused ? align256(qgemm_ws_bytes(wtype, M, N, K)) : align256((size_t)N * K * 2);
+    const bool stage_x = xtype == VKF_X_Q8_1 || ((uintptr_t)X & 15) || (ldx * 2) % 16;
+    uint8_t *scr = (uint8_t *)stream_scratch(stream, (stage_x ? xbytes : 0) + wbytes);
     if (!scr) return VKF_ERR_NOMEM;
-    int rc = dequant_launch(W, scr, (uint64_t)N * K / vkf_qtype_block_values(wtype), wtype, stream, true);
-    if (rc) return rc;
     const void *xf = X;
     int64_t lda = ldx;
-    if (xtype == VKF_X_Q8_1) {
-        rc = q8_1_to_f16(X, scr + wbytes, M, K, ldx, K, stream);
+    if (stage_x) {
+        int rc = VKF_OK;
+        if (xtype == VKF_X_Q8_1) rc = q8_1_to_f16(X, scr, M, K, ldx, K, stream);
+        else if (cudaMemcpy2DAsync(scr, (size_t)K * 2, X, ldx * 2, (size_t)K * 2, M, cudaMemcpyDeviceToDevice,
+                                   stream) != cudaSuccess)
+            rc = VKF_ERR_CUDA;
         if (rc) return rc;
-        xf = scr + wbytes;
-        lda = K;
-    } else if (((uintptr_t)X & 15) || (ldx * 2) % 16) {
-        if (cudaMemcpy2DAsync(scr + wbytes, (size_t)K * 2, X, ldx * 2, (size_t)K * 2, M, cudaMemcpyDeviceToDevice,
-                              stream) != cudaSuccess)
-            return VKF_ERR_CUDA;
-        xf = scr + wbytes;
+        xf = scr;
         lda = K;
     }
-    if (((size_t)K * 2) % 16) return VKF_ERR_UNSUPPORTED;
-    return gemm_f16_tn(xf, lda, scr, K, M, N, K, 1.0f, 0.0f, nullptr, 0, 0, nullptr, 0, Y, ldy,
+    uint8_t *wf = scr + (stage_x ? xbytes : 0);
+    if (fused) return qgemm_launch(wtype, W, xf, lda, Y, ytype == VKF_Y_F16, ldy, M, N, K, (float *)wf, stream);
+    int rc = dequant_launch(W, wf, (uint64_t)N * K / vkf_qtype_block_values(wtype), wtype, stream, true);
+    if (rc) return rc;
+    return gemm_f16_tn(xf, lda, wf, K, M, N, K, 1.0f, 0.0f, nullptr, 0, 0, nullptr, 0, Y, ldy,
                        ytype == VKF_Y_F16, stream);
 }
 

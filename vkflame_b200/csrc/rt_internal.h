@@ -1,6 +1,7 @@
 // rt_internal.h — shared host-side state of libvkflame_rt (not installed).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stddef.h>
@@ -41,6 +42,21 @@ int validate_device_range(const void *p, size_t bytes);
 
 bool debug_enabled();
 void log(const char *fmt, ...);
+
+// Tensor maps (false if the shape or alignment is not encodable):
+// K-major operand of esize-byte elements [rows x cols], row stride ld
+// elements, box = 128 bytes of K x box_rows, 128-byte swizzle (the tcgen05
+// operand layout);
+bool make_kmajor_map(CUtensorMap *m, const void *base, int esize, int64_t rows, int64_t cols, int64_t ld,
+                     int box_rows);
+// row-major fp16 (esize 2) or fp32 (4) matrix [rows x cols], row stride ld
+// elements, box = box_rows x box_cols, no swizzle (tile stores);
+bool make_rowmajor_map(CUtensorMap *m, const void *base, int esize, int64_t rows, int64_t cols, int64_t ld,
+                       int box_cols, int box_rows);
+// byte matrix [rows x row_bytes] (16-byte multiple) as 8-byte elements, box
+// = box_rows x box_bytes, no swizzle.
+bool make_byte_matrix_map(CUtensorMap *m, const void *base, int64_t rows, int64_t row_bytes, int box_bytes,
+                          int box_rows);
 
 }  // namespace vkf
 

@@ -103,5 +103,24 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, 
         : "memory");
 }
 
+// 2-D TMA tile store from shared memory (no multicast); elements outside the
+// tensor are not written.  Completion is tracked by bulk groups.
+__device__ __forceinline__ void tma_store_2d(const void *tmap, const void *src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+                 "r"(smem_addr(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed bulk groups still READ their shared source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until every committed bulk group has completed (writes performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA / tensor core) accesses.
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 }  // namespace tc
 }  // namespace vkf
