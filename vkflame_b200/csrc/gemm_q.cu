@@ -58,7 +58,11 @@ namespace qgemm {
 constexpr int BW = 128;   // weight rows per tile (MMA M, TMEM lanes)
 constexpr int KV = 64;    // K values per MMA stage (128 bytes of fp16 per row)
 constexpr int RV = 256;   // K values per packed-weight stage (the work unit)
-constexpr int CV = 8;     // converter warps
+#ifndef VKF_QGEMM_CV
+#define VKF_QGEMM_CV 8
+#endif
+constexpr int CV = VKF_QGEMM_CV;  // converter warps
+constexpr int RPL = BW / (8 * CV);  // rows per converter lane (8 row groups of 4 lanes per warp)
 constexpr int W_RAW = 6, W_CONV = 7;
 constexpr int NT = 32 * (W_CONV + CV);
 constexpr int A_BYTES = BW * 128;
@@ -91,6 +95,7 @@ struct Params {
     int64_t ldy;
     int y_f16;
     int y_tma;        // Y written by 2-D tensor stores (16-byte aligned rows)
+    int prefetch;     // W written by no kernel: stream it before the dependency wait
     int units;        // tiles x (K / 256)
     float *ws;        // per CTA: [NB*BX/4][128][4] fp32 partials (4-column groups)
     int *flags;       // [grid] partial published (reset by the consumer)
@@ -305,8 +310,13 @@ __global__ void __launch_bounds__(NT, 1)
     const long long t_start = clock64();
 #endif
 
+    // Programmatic dependent launch: dependents may start their set-up now.
+    // Everything another kernel may write (X, Y, the scratch partials and
+    // flags, and W unless it is static) is touched only after the wait.
+    asm volatile("griddepcontrol.launch_dependents;");
     if (warp == 0) {
         // ---- X tiles: NB boxes of BX rows per K-block ----
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         if (lane == 0) {
             int g = 0;
             bool ok = true;
@@ -331,6 +341,7 @@ __global__ void __launch_bounds__(NT, 1)
         }
     } else if (warp == W_RAW) {
         // ---- packed weight bytes: one tensor copy per 128 rows x 256 values ----
+        if (!p.prefetch) asm volatile("griddepcontrol.wait;" ::: "memory");
         if (lane == 0) {
             int g = 0;
             bool ok = true;
@@ -350,9 +361,9 @@ __global__ void __launch_bounds__(NT, 1)
         // ---- converters: warp cw owns rows 16 cw .. 16 cw + 15 ----
         const int cw = warp - W_CONV;
         const int cp = lane & 3;
-        int rows[2];
+        int rows[RPL];
 #pragma unroll
-        for (int i = 0; i < 2; ++i) rows[i] = 16 * cw + 8 * i + row_of_group<QT>(lane >> 2);
+        for (int i = 0; i < RPL; ++i) rows[i] = (BW / CV) * cw + 8 * i + row_of_group<QT>(lane >> 2);
         int g = 0, gr = 0;
         bool ok = true;
         for (int u = u_begin; u < u_end && ok; ++u, ++gr) {
@@ -374,7 +385,7 @@ __global__ void __launch_bounds__(NT, 1)
                 QT_T0;
                 uint8_t *at = smem + s * STAGE;
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
+                for (int i = 0; i < RPL; ++i) {
                     const int r = rows[i];
 #ifndef VKF_QGEMM_NOCONV
                     uint4 va, vb;
@@ -442,6 +453,7 @@ __global__ void __launch_bounds__(NT, 1)
     } else {
         // ---- epilogue (warps 2..5): TMEM lane = weight row = output column ----
         const int q = warp & 3;
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         const int tid = threadIdx.x - 64;  // 0..127 over the four epilogue warps
         int it = 0;
         uint32_t ybuf = 0;  // Y staging buffers used so far
@@ -626,7 +638,7 @@ static int grid_for(int units) {
 
 template <int QT, int BX, int NB>
 static int launch(const void *W, const void *X, int64_t ldx, void *Y, int y_f16, int64_t ldy, int M, int N, int K,
-                  float *ws, cudaStream_t stream) {
+                  float *ws, int prefetch, cudaStream_t stream) {
     using C = Cfg<QT, BX, NB>;
     static_assert(C::FITS, "ring does not fit shared memory");
     constexpr int NC = BX * NB;
@@ -655,8 +667,18 @@ static int launch(const void *W, const void *X, int64_t ldx, void *Y, int y_f16,
     memset(&ty, 0, sizeof(ty));
     const int esize = y_f16 ? 2 : 4;
     const int y_tma = make_rowmajor_map(&ty, Y, esize, M, N, ldy, BW, EPI_BUF / (BW * esize)) ? 1 : 0;
-    Params p{M, N, K, Y, ldy, y_f16, y_tma, units, ws, flags, ds->d_error};
-    kern<<<grid, NT, C::SMEM, stream>>>(tx, tw, ty, p);
+    Params p{M, N, K, Y, ldy, y_f16, y_tma, prefetch, units, ws, flags, ds->d_error};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(NT);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = stream;
+    cudaLaunchAttribute la[1];
+    la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    la[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = la;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, tx, tw, ty, p);
     return check_launch();
 }
 
@@ -665,15 +687,15 @@ static int launch(const void *W, const void *X, int64_t ldx, void *Y, int y_f16,
 // Q8_0, whose 34 KB packed stages leave no room for a 512-column ring.
 template <int QT>
 static int launch_q(const void *W, const void *X, int64_t ldx, void *Y, int y_f16, int64_t ldy, int M, int N, int K,
-                    float *ws, cudaStream_t stream) {
+                    float *ws, int prefetch, cudaStream_t stream) {
     switch (tile_cols<QT>(M)) {
     case 512:
-        if constexpr (Cfg<QT, 256, 2>::FITS) return launch<QT, 256, 2>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
+        if constexpr (Cfg<QT, 256, 2>::FITS) return launch<QT, 256, 2>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
         return VKF_ERR_UNSUPPORTED;
-    case 256: return launch<QT, 256, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
-    case 128: return launch<QT, 128, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
-    case 64: return launch<QT, 64, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
-    default: return launch<QT, 32, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
+    case 256: return launch<QT, 256, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
+    case 128: return launch<QT, 128, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
+    case 64: return launch<QT, 64, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
+    default: return launch<QT, 32, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
     }
 }
 
@@ -708,15 +730,17 @@ size_t qgemm_ws_bytes(int wtype, int M, int N, int K) {
 }
 
 // ws: at least qgemm_ws_bytes(...) of device scratch, 16-byte aligned.
+// prefetch: W is written by no kernel (static model weights), so its bytes
+// may stream while the previous kernel on the stream finishes.
 int qgemm_launch(int wtype, const void *W, const void *X, int64_t ldx, void *Y, int y_f16, int64_t ldy, int M, int N,
-                 int K, float *ws, cudaStream_t stream) {
+                 int K, float *ws, int prefetch, cudaStream_t stream) {
     if (!qgemm_supported(wtype, W, K) || ((uintptr_t)X & 15) || (ldx * 2) % 16) return VKF_ERR_UNSUPPORTED;
     if ((int64_t)((M + 511) / 512) * ((N + 127) / 128) * (K / qgemm::RV) > INT32_MAX / 2) return VKF_ERR_UNSUPPORTED;
     switch (wtype) {
-    case VKF_DEQUANT_Q4_0: return qgemm::launch_q<VKF_DEQUANT_Q4_0>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
-    case VKF_DEQUANT_Q8_0: return qgemm::launch_q<VKF_DEQUANT_Q8_0>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
-    case VKF_DEQUANT_Q4_K: return qgemm::launch_q<VKF_DEQUANT_Q4_K>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
-    case VKF_DEQUANT_Q5_K: return qgemm::launch_q<VKF_DEQUANT_Q5_K>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, stream);
+    case VKF_DEQUANT_Q4_0: return qgemm::launch_q<VKF_DEQUANT_Q4_0>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
+    case VKF_DEQUANT_Q8_0: return qgemm::launch_q<VKF_DEQUANT_Q8_0>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
+    case VKF_DEQUANT_Q4_K: return qgemm::launch_q<VKF_DEQUANT_Q4_K>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
+    case VKF_DEQUANT_Q5_K: return qgemm::launch_q<VKF_DEQUANT_Q5_K>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
     default: return VKF_ERR_UNSUPPORTED;
     }
 }

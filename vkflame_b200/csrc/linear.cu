@@ -31,7 +31,7 @@ int gemm_f16_tn(const void *A, int64_t lda, const void *B, int64_t ldb, int M, i
 bool qgemm_supported(int wtype, const void *W, int K);
 size_t qgemm_ws_bytes(int wtype, int M, int N, int K);
 int qgemm_launch(int wtype, const void *W, const void *X, int64_t ldx, void *Y, int y_f16, int64_t ldy, int M, int N,
-                 int K, float *ws, cudaStream_t stream);
+                 int K, float *ws, int prefetch, cudaStream_t stream);
 int transpose(const void *src, int64_t lds, void *dst, int64_t ldd, int rows, int cols, int esize,
               cudaStream_t stream);
 
@@ -62,7 +62,7 @@ static bool fused_prefill_enabled() {
 // the fused-dequant tcgen05 GEMM (W read once as packed blocks); otherwise W
 // is widened to fp16 (one rounding per weight) and the f16 tcgen05 GEMM runs.
 static int quant_linear_gemm(const void *W, int wtype, const void *X, int xtype, void *Y, int ytype, int M, int N,
-                             int K, int64_t ldx, int64_t ldy, cudaStream_t stream) {
+                             int K, int64_t ldx, int64_t ldy, cudaStream_t stream, unsigned flags) {
     if (((size_t)K * 2) % 16) return VKF_ERR_UNSUPPORTED;
     const bool fused = fused_prefill_enabled() && qgemm_supported(wtype, W, K);
     // Staged X, then the widened W (widen path) or the split-tile partials
@@ -85,7 +85,9 @@ static int quant_linear_gemm(const void *W, int wtype, const void *X, int xtype,
         lda = K;
     }
     uint8_t *wf = scr + (stage_x ? xbytes : 0);
-    if (fused) return qgemm_launch(wtype, W, xf, lda, Y, ytype == VKF_Y_F16, ldy, M, N, K, (float *)wf, stream);
+    if (fused)
+        return qgemm_launch(wtype, W, xf, lda, Y, ytype == VKF_Y_F16, ldy, M, N, K, (float *)wf,
+                            (flags & VKF_FLAG_STATIC_WEIGHTS) ? 1 : 0, stream);
     int rc = dequant_launch(W, wf, (uint64_t)N * K / vkf_qtype_block_values(wtype), wtype, stream, true);
     if (rc) return rc;
     return gemm_f16_tn(xf, lda, wf, K, M, N, K, 1.0f, 0.0f, nullptr, 0, 0, nullptr, 0, Y, ldy,
@@ -165,7 +167,7 @@ int quant_linear(const void *W, int wtype, const void *X, int xtype, void *Y, in
     if ((wtype == VKF_DEQUANT_Q4_K || wtype == VKF_DEQUANT_Q5_K) ? (wa & 3) : (wa & 1)) return VKF_ERR_BADPTR;
     if ((uintptr_t)Y & (ytype == VKF_Y_F16 ? 1 : 3)) return VKF_ERR_BADPTR;
     if (xtype == VKF_X_F16 && ((uintptr_t)X & 1)) return VKF_ERR_BADPTR;
-    if (M > gemv_max_m()) return quant_linear_gemm(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, stream);
+    if (M > gemv_max_m()) return quant_linear_gemm(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, stream, flags);
     return quant_linear_gemv(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, stream, flags);
 }
 

@@ -12,30 +12,66 @@
 namespace vkf {
 namespace {
 
+// Four threads per 32-value block, eight values each (two 16-byte loads when
+// x rows are 16-byte aligned): max and sum by shuffles inside the 4-lane
+// group, eight codes stored as two 4-byte words (2-byte halves when y is
+// only 2-byte aligned).  Same IEEE-rounded operations per value as the
+// oracle.  vec bits: 1 = vector loads, 2 = y 4-byte aligned.
 __global__ void __launch_bounds__(256) quantize_q8_1_kernel(const float *__restrict__ x, uint8_t *__restrict__ y,
-                                                            int M, int K, int64_t ldx) {
-    const int lane = threadIdx.x & 31;
-    const int64_t blk = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+                                                            int M, int K, int64_t ldx, int vec) {
+    const int64_t t = (int64_t)blockIdx.x * 256 + threadIdx.x;
+    const int qtr = threadIdx.x & 3;
     const int nbr = K / 32;
-    if (blk >= (int64_t)M * nbr) return;
-    const int64_t m = blk / nbr, b = blk % nbr;
-    const float v = x[m * ldx + b * 32 + lane];
-    float amax = fabsf(v);
+    const int64_t blk = t >> 2;
+    const bool on = blk < (int64_t)M * nbr;  // whole 4-lane groups share `on`
+    const int64_t m = on ? blk / nbr : 0, b = on ? blk % nbr : 0;
+    float v[8];
+    if (on) {
+        const float *src = x + m * ldx + b * 32 + 8 * qtr;
+        if (vec & 1) {
+            const float4 a0 = __ldg(reinterpret_cast<const float4 *>(src)), a1 = __ldg(reinterpret_cast<const float4 *>(src) + 1);
+            v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w; v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+        } else {
 #pragma unroll
-    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float d = __fdiv_rn(amax, 127.0f);
-    int q = 0;
-    if (d != 0.0f) {
-        q = (int)roundf(__fdiv_rn(v, d));
-        q = max(-127, min(127, q));
+            for (int i = 0; i < 8; ++i) v[i] = src[i];
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.f;
     }
-    int sum = q;
+    float amax = 0.f;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float d = __fdiv_rn(amax, 127.0f);
+    int sum = 0;
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        int q = 0;
+        if (d != 0.0f) {
+            q = (int)roundf(__fdiv_rn(v[i], d));
+            q = max(-127, min(127, q));
+        }
+        sum += q;
+        w[i >> 2] |= (uint32_t)(q & 0xFF) << (8 * (i & 3));
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if (!on) return;
     uint8_t *out = y + blk * 36;
-    out[4 + lane] = (uint8_t)(int8_t)q;
-    if (lane == 0) {
-        __half hd = __float2half_rn(d), hs = __float2half_rn(__fmul_rn(d, (float)sum));
+    if (vec & 2) {  // y 4-byte aligned
+        uint32_t *codes = reinterpret_cast<uint32_t *>(out + 4 + 8 * qtr);
+        codes[0] = w[0];
+        codes[1] = w[1];
+    } else {
+        uint16_t *codes = reinterpret_cast<uint16_t *>(out + 4 + 8 * qtr);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) codes[i] = (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
+    }
+    if (qtr == 0) {
+        const __half hd = __float2half_rn(d), hs = __float2half_rn(__fmul_rn(d, (float)sum));
         *reinterpret_cast<__half *>(out) = hd;
         *reinterpret_cast<__half *>(out + 2) = hs;
     }
@@ -47,6 +83,10 @@ __global__ void __launch_bounds__(256) quantize_q8_1_kernel(const float *__restr
 // store.  Grid: (blocks of a row / 64, M).
 __global__ void __launch_bounds__(256) q8_1_to_f16_kernel(const uint8_t *__restrict__ src, __half *__restrict__ dst,
                                                           int M, int K, int64_t ldb, int64_t ldo) {
+    // Programmatic dependent launch: the next kernel (the GEMM) may start its
+    // set-up now; src is read only after the previous kernel completed.
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int nbr = K / 32;
     const int i = blockIdx.x * 256 + threadIdx.x;  // (block, quarter) within the row
     const int b = i >> 2, qtr = i & 3;
@@ -81,14 +121,24 @@ int q8_1_to_f16(const void *src, void *dst, int M, int K, int64_t ldb, int64_t l
     if (M == 0 || nbr == 0) return VKF_OK;
     if (M > 65535) return VKF_ERR_UNSUPPORTED;
     const dim3 grid((unsigned)((nbr * 4 + 255) / 256), (unsigned)M);
-    q8_1_to_f16_kernel<<<grid, 256, 0, stream>>>((const uint8_t *)src, (__half *)dst, M, K, ldb, ldo);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, q8_1_to_f16_kernel, (const uint8_t *)src, (__half *)dst, M, K, ldb, ldo);
     return check_launch();
 }
 
 int quantize_q8_1_launch(const float *x, void *y, int M, int K, int64_t ldx, cudaStream_t stream) {
     int64_t blocks = (int64_t)M * (K / 32);
     if (blocks == 0) return VKF_OK;
-    quantize_q8_1_kernel<<<(unsigned)((blocks + 7) / 8), 256, 0, stream>>>(x, (uint8_t *)y, M, K, ldx);
+    const int vec = (((uintptr_t)x & 15) == 0 && ldx % 4 == 0 ? 1 : 0) | (((uintptr_t)y & 3) == 0 ? 2 : 0);
+    quantize_q8_1_kernel<<<(unsigned)((blocks * 4 + 255) / 256), 256, 0, stream>>>(x, (uint8_t *)y, M, K, ldx, vec);
     return check_launch();
 }
 
