@@ -214,6 +214,93 @@ __device__ __forceinline__ void convert16(const uint8_t *rp, int kk, int cp, uin
     ob = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
+// 32 values (32-value block / sub-block B, 0..7, of the 256-value stage) of
+// one row, as 16 fp16 pairs in K order, for the TMEM-resident A operand.
+// rp is the row's stage (16-byte aligned: row pitches are 16-byte
+// multiples); loads are 16-byte and, with one row per lane and odd pitches in
+// 16-byte units, bank-conflict free.  Same arithmetic as convert16.
+template <int QT, int B>
+__device__ __forceinline__ void convert32(const uint8_t *rp, uint32_t (&o)[16]) {
+    if constexpr (QT == VKF_DEQUANT_Q8_0) {
+        constexpr int A0 = (34 * B) & ~15, OFF = 34 * B - A0, NV = (OFF + 34 + 15) / 16;
+        uint32_t w[4 * NV + 1] = {};  // +1: the funnel shift's upper word past the window (shift 0 there)
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const uint4 t = *reinterpret_cast<const uint4 *>(rp + A0 + 16 * i);
+            w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
+        }
+        const uint32_t dw = w[OFF / 4] >> (8 * (OFF % 4));
+        const __half2 d2 = __half2half2(__ushort_as_half((unsigned short)(dw & 0xFFFF)));
+        const __half2 off = __float2half2_rn(1152.0f);
+        constexpr int C0 = OFF + 2;  // first code byte in the window
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t x = __funnelshift_r(w[C0 / 4 + j], w[C0 / 4 + j + 1], 8 * (C0 % 4)) ^ 0x80808080u;
+            o[2 * j] = h2u(__hmul2(__hsub2(u2h(__byte_perm(x, 0x64646464u, 0x4140)), off), d2));
+            o[2 * j + 1] = h2u(__hmul2(__hsub2(u2h(__byte_perm(x, 0x64646464u, 0x4342)), off), d2));
+        }
+    } else if constexpr (QT == VKF_DEQUANT_Q4_0) {
+        constexpr int A0 = (18 * B) & ~15, OFF = 18 * B - A0, NV = (OFF + 18 + 15) / 16;
+        uint32_t w[4 * NV + 1] = {};
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const uint4 t = *reinterpret_cast<const uint4 *>(rp + A0 + 16 * i);
+            w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
+        }
+        const uint32_t dw = w[OFF / 4] >> (8 * (OFF % 4));
+        const __half2 d2 = __half2half2(__ushort_as_half((unsigned short)(dw & 0xFFFF)));
+        const __half2 off = __float2half2_rn(1032.0f);
+        constexpr int C0 = OFF + 2;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {  // code bytes 4j..4j+3: values 4j.. (low), 16+4j.. (high)
+            const uint32_t x = __funnelshift_r(w[C0 / 4 + j], w[C0 / 4 + j + 1], 8 * (C0 % 4));
+            const uint32_t p0 = __byte_perm(x, 0, 0x4140), p1 = __byte_perm(x, 0, 0x4342);
+            o[2 * j] = h2u(__hmul2(__hsub2(u2h((p0 & 0x000F000Fu) | 0x64006400u), off), d2));
+            o[2 * j + 1] = h2u(__hmul2(__hsub2(u2h((p1 & 0x000F000Fu) | 0x64006400u), off), d2));
+            o[8 + 2 * j] = h2u(__hmul2(__hsub2(u2h(((p0 >> 4) & 0x000F000Fu) | 0x64006400u), off), d2));
+            o[8 + 2 * j + 1] = h2u(__hmul2(__hsub2(u2h(((p1 >> 4) & 0x000F000Fu) | 0x64006400u), off), d2));
+        }
+    } else {  // Q4_K / Q5_K: sub-block B = low (B even) or high (B odd) nibbles of qs[32 (B/2) ..]
+        constexpr bool Q5 = QT == VKF_DEQUANT_Q5_K;
+        const uint4 hd = *reinterpret_cast<const uint4 *>(rp);
+        const uint32_t sw[3] = {hd.y, hd.z, hd.w};  // the 12 scale bytes
+        auto sb = [&](int i) { return (int)((sw[i >> 2] >> (8 * (i & 3))) & 0xFF); };
+        int sc, mn;
+        if constexpr (B < 4) {
+            sc = sb(B) & 63;
+            mn = sb(B + 4) & 63;
+        } else {
+            sc = (sb(B + 4) & 0xF) | ((sb(B - 4) >> 6) << 4);
+            mn = (sb(B + 4) >> 4) | ((sb(B) >> 6) << 4);
+        }
+        const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFF)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+        const float dd = d * (float)sc, mm = dmin * (float)mn;  // exact products
+        constexpr int QO = (Q5 ? 48 : 16) + 32 * (B / 2);
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(rp + QO), q1 = *reinterpret_cast<const uint4 *>(rp + QO + 16);
+        const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        uint32_t hw[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+        if constexpr (Q5) {
+            const uint4 h0 = *reinterpret_cast<const uint4 *>(rp + 16), h1 = *reinterpret_cast<const uint4 *>(rp + 32);
+            const uint32_t hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) hw[i] = ((hv[i] >> B) & 0x01010101u) << 4;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t c = ((qw[i] >> (4 * (B & 1))) & 0x0F0F0F0Fu) | hw[i];
+            float f[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float qf = __uint_as_float(0x4B000000u | ((c >> (8 * e)) & 0xFFu)) - 8388608.0f;
+                f[e] = fmaf(dd, qf, -mm);
+            }
+            o[2 * i] = h2u(__floats2half2_rn(f[0], f[1]));
+            o[2 * i + 1] = h2u(__floats2half2_rn(f[2], f[3]));
+        }
+    }
+}
+
 // Row (within a group of 8) served by lane group g = lane >> 2, ordered so
 // that each 8-lane store phase writes 8 distinct 16-byte bank groups of the
 // swizzled tile: chunk sets {2cp} (Q8_0) pair rows r, r^1; {cp} (K-quants)
@@ -249,18 +336,23 @@ __device__ __forceinline__ bool epi_all(bool v) {
     return r != 0;
 }
 
-template <int QT, int BX, int NB, int NS, int RS>
+template <int QT, int BX, int NB, int NS, int RS, bool ATM>
 __global__ void __launch_bounds__(NT, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                  const __grid_constant__ CUtensorMap tmY, const __grid_constant__ Params p) {
     constexpr int RB = Packed<QT>::RB;
     constexpr int NC = NB * BX;  // accumulator columns per tile
-    constexpr int B_BYTES = NC * 128, STAGE = A_BYTES + B_BYTES;
+    // ATM: the converted weight tile lives in TMEM (NS stages x 32 columns
+    // after the accumulators) instead of shared memory.
+    constexpr int BOFF = ATM ? 0 : A_BYTES;  // X tile offset within a stage
+    constexpr int B_BYTES = NC * 128, STAGE = BOFF + B_BYTES;
     constexpr int RAW_BYTES = (BW * RB + 127) / 128 * 128;
-    constexpr int NBUF = 2 * NC <= 512 ? 2 : 1;
+    constexpr int A_COLS = ATM ? NS * 32 : 0;
+    constexpr int NBUF = 2 * NC + A_COLS <= 512 ? 2 : 1;
+    static_assert(NC + A_COLS <= 512, "TMEM columns");
+    constexpr int TNEED = NBUF * NC + A_COLS;
     constexpr uint32_t IDESC = tc::instr_desc(tc::KIND_F16, BW, BX);
-    constexpr uint32_t TCOLS = NBUF * NC <= 32 ? 32 : NBUF * NC <= 64 ? 64 : NBUF * NC <= 128 ? 128
-                             : NBUF * NC <= 256 ? 256 : 512;
+    constexpr uint32_t TCOLS = TNEED <= 32 ? 32 : TNEED <= 64 ? 64 : TNEED <= 128 ? 128 : TNEED <= 256 ? 256 : 512;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *raw = smem + NS * STAGE;
@@ -334,7 +426,7 @@ __global__ void __launch_bounds__(NT, 1)
                     mbar_arrive_expect_tx(&ab_full[s], B_BYTES);
 #pragma unroll
                     for (int h = 0; h < NB; ++h)
-                        tc::tma_load_2d(smem + s * STAGE + A_BYTES + h * BX * 128, &tmX, kb * KV, m0 + h * BX,
+                        tc::tma_load_2d(smem + s * STAGE + BOFF + h * BX * 128, &tmX, kb * KV, m0 + h * BX,
                                         &ab_full[s]);
                 }
             }
@@ -356,6 +448,53 @@ __global__ void __launch_bounds__(NT, 1)
                     tc::tma_load_2d(raw + s * RAW_BYTES, &tmW, kr * (RB / 8), n0, &raw_full[s]);
                 }
             }
+        }
+    } else if (warp >= W_CONV && ATM) {
+        // ---- converters, TMEM form: warp owns TMEM lane quarter warp % 4
+        // (rows 32 q .. 32 q + 31, one row per lane) and half h of each
+        // K-block's 64 values; one tcgen05.st of 16 columns per K-block ----
+        const int qq = warp & 3, h = (warp - W_CONV) >> 2;
+        const int row = 32 * qq + lane;
+        const uint32_t ta0 = tmem0 + ((uint32_t)(32 * qq) << 16) + NBUF * NC + 16 * h;
+        int g = 0, gr = 0;
+        bool ok = true;
+        for (int u = u_begin; u < u_end && ok; ++u, ++gr) {
+            const int rs = gr % RS;
+            {
+                QT_T0;
+                if (!(ok = mbar_wait(&raw_full[rs], (gr / RS) & 1, p.err))) break;
+                QT_ACC(0);
+            }
+            const uint8_t *rp = raw + rs * RAW_BYTES + row * RB;
+            auto kblock = [&](auto kk_c) {
+                constexpr int KK = decltype(kk_c)::value;
+                const int s = g % NS;
+                if (ok) {
+                    QT_T0;
+                    if (g >= NS) ok = mbar_wait(&ab_empty[s], ((g / NS) & 1) ^ 1, p.err);
+                    QT_ACC(1);
+                }
+                if (ok) {
+                    QT_T0;
+                    tc::fence_after_sync();  // the MMAs that read this TMEM stage are complete
+                    uint32_t o[16];
+                    if (h == 0) convert32<QT, 2 * KK>(rp, o);
+                    else convert32<QT, 2 * KK + 1>(rp, o);
+                    tc::tmem_st16(ta0 + 32 * s, o);
+                    tc::tmem_wait_st();
+                    tc::fence_before_sync();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&ab_full[s]);
+                    QT_ACC(2);
+                }
+                ++g;
+            };
+            kblock(std::integral_constant<int, 0>{});
+            kblock(std::integral_constant<int, 1>{});
+            kblock(std::integral_constant<int, 2>{});
+            kblock(std::integral_constant<int, 3>{});
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[rs]);
         }
     } else if (warp >= W_CONV) {
         // ---- converters: warp cw owns rows 16 cw .. 16 cw + 15 ----
@@ -434,14 +573,18 @@ __global__ void __launch_bounds__(NT, 1)
                         QT_ACC(3);
                     }
                     tc::fence_after_sync();
-                    const uint32_t sa = smem_addr(smem + s * STAGE), sb = sa + A_BYTES;
+                    const uint32_t sa = smem_addr(smem + s * STAGE), sb = sa + BOFF;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
-                        for (int h = 0; h < NB; ++h)
-                            tc::mma<tc::KIND_F16>(tmem + h * BX, tc::smem_desc_sw128(sa + kk * 32),
-                                                  tc::smem_desc_sw128(sb + h * BX * 128 + kk * 32), IDESC,
-                                                  (kb > kb0 || kk) ? 1u : 0u);
+                        for (int h = 0; h < NB; ++h) {
+                            const uint64_t bd = tc::smem_desc_sw128(sb + h * BX * 128 + kk * 32);
+                            const uint32_t acc = (kb > kb0 || kk) ? 1u : 0u;
+                            if constexpr (ATM)
+                                tc::mma_f16_ta(tmem + h * BX, tmem0 + NBUF * NC + 32 * s + 8 * kk, bd, IDESC, acc);
+                            else
+                                tc::mma<tc::KIND_F16>(tmem + h * BX, tc::smem_desc_sw128(sa + kk * 32), bd, IDESC, acc);
+                        }
                     tc::commit(&ab_empty[s]);
                 }
                 tc::commit(&acc_full[b]);
@@ -606,26 +749,41 @@ __global__ void __launch_bounds__(NT, 1)
     }
 }
 
-template <int QT, int BX, int NB>
+#ifndef VKF_QGEMM_ATM
+#define VKF_QGEMM_ATM 1
+#endif
+constexpr bool ATM_DEFAULT = VKF_QGEMM_ATM != 0;
+
+template <int QT, int BX, int NB, bool ATM = ATM_DEFAULT>
 struct Cfg {
     static constexpr int RB = Packed<QT>::RB;
     static constexpr int RAW_BYTES = (BW * RB + 127) / 128 * 128;
-    static constexpr int STAGE = A_BYTES + NB * BX * 128;
+    static constexpr int STAGE = (ATM ? 0 : A_BYTES) + NB * BX * 128;
     static constexpr int FIXED = 1024 + 256 + 2 * EPI_BUF;
+#ifndef VKF_QGEMM_NSMAX
+#define VKF_QGEMM_NSMAX 4
+#endif
     // Deepest A/B ring (<= 4) that still leaves two packed stages, then as
     // many packed stages (<= 6) as fit.
-    static constexpr int NS = (SMEM_CAP - FIXED - 2 * RAW_BYTES) / STAGE >= 4 ? 4
+    static constexpr int NS = (SMEM_CAP - FIXED - 2 * RAW_BYTES) / STAGE >= VKF_QGEMM_NSMAX ? VKF_QGEMM_NSMAX
                               : (SMEM_CAP - FIXED - 2 * RAW_BYTES) / STAGE;
     static constexpr int RS0 = (SMEM_CAP - FIXED - NS * STAGE) / RAW_BYTES;
     static constexpr int RS = RS0 > 6 ? 6 : RS0;
     static constexpr size_t SMEM = (size_t)NS * STAGE + (size_t)RS * RAW_BYTES + FIXED;
-    static constexpr bool FITS = NS >= 2 && RS >= 2;
+    // TMEM: accumulator columns plus, with ATM, 32 columns per stage
+    static constexpr bool FITS = NS >= 2 && RS >= 2 && (!ATM || (NB * BX + NS * 32 <= 512 && CV == 8));
 };
 
-// Columns per tile (NB x BX) for M activation rows; mirrors launch_q.
+// Columns per tile (NB x BX) for M activation rows; mirrors launch_q.  Up
+// to 256 the converted weight tile lives in TMEM (no shared-memory traffic
+// for it); above 256, where the 512-column accumulator leaves no TMEM for
+// it, the shared-memory form with one weight decode per 512 activation rows
+// is faster (Q4_K 5120 x 13824, M = 512: 86 against 106 us for two 256-row
+// tiles in the TMEM form), except Q8_0, whose packed stages leave no room
+// for a 512-column ring.
 template <int QT>
 static int tile_cols(int M) {
-    if constexpr (Cfg<QT, 256, 2>::FITS) {
+    if constexpr (Cfg<QT, 256, 2, false>::FITS) {
         if (M > 256) return 512;
     }
     return M > 128 ? 256 : M > 64 ? 128 : M > 32 ? 64 : 32;
@@ -636,17 +794,17 @@ static int grid_for(int units) {
     return std::max(1, std::min(units, ds ? ds->sm_count : 148));
 }
 
-template <int QT, int BX, int NB>
+template <int QT, int BX, int NB, bool ATM>
 static int launch(const void *W, const void *X, int64_t ldx, void *Y, int y_f16, int64_t ldy, int M, int N, int K,
                   float *ws, int prefetch, cudaStream_t stream) {
-    using C = Cfg<QT, BX, NB>;
+    using C = Cfg<QT, BX, NB, ATM>;
     static_assert(C::FITS, "ring does not fit shared memory");
     constexpr int NC = BX * NB;
     const int64_t row_bytes = (int64_t)K / RV * C::RB;
     CUtensorMap tx, tw;
     if (!make_kmajor_map(&tx, X, 2, M, K, ldx, BX) || !make_byte_matrix_map(&tw, W, N, row_bytes, C::RB, BW))
         return VKF_ERR_UNSUPPORTED;
-    auto kern = qgemm_kernel<QT, BX, NB, C::NS, C::RS>;
+    auto kern = qgemm_kernel<QT, BX, NB, C::NS, C::RS, ATM>;
     static bool attr[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -690,12 +848,13 @@ static int launch_q(const void *W, const void *X, int64_t ldx, void *Y, int y_f1
                     float *ws, int prefetch, cudaStream_t stream) {
     switch (tile_cols<QT>(M)) {
     case 512:
-        if constexpr (Cfg<QT, 256, 2>::FITS) return launch<QT, 256, 2>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
+        if constexpr (Cfg<QT, 256, 2, false>::FITS)
+            return launch<QT, 256, 2, false>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
         return VKF_ERR_UNSUPPORTED;
-    case 256: return launch<QT, 256, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
-    case 128: return launch<QT, 128, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
-    case 64: return launch<QT, 64, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
-    default: return launch<QT, 32, 1>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
+    case 256: return launch<QT, 256, 1, ATM_DEFAULT>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
+    case 128: return launch<QT, 128, 1, ATM_DEFAULT>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
+    case 64: return launch<QT, 64, 1, ATM_DEFAULT>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
+    default: return launch<QT, 32, 1, ATM_DEFAULT>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
     }
 }
 

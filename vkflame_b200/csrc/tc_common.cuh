@@ -103,6 +103,28 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, 
         : "memory");
 }
 
+// MMA with the A operand in tensor memory (M = 128 rows = lanes, K packed two
+// 16-bit values per 32-bit column) and B from shared memory.
+__device__ __forceinline__ void mma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc));
+}
+
+// Thread l of the warp writes 16 consecutive 32-bit columns of lane
+// (taddr.lane + l); followed by wait::st before the data is signalled.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // 2-D TMA tile store from shared memory (no multicast); elements outside the
 // tensor are not written.  Completion is tracked by bulk groups.
 __device__ __forceinline__ void tma_store_2d(const void *tmap, const void *src, int x, int y) {
