@@ -175,12 +175,16 @@ __device__ __forceinline__ void convert16(const uint8_t *rp, int kk, int cp, uin
         // chunk cp = low nibbles (sub-block 2kk), cp + 4 = high nibbles (2kk + 1)
         constexpr bool Q5 = QT == VKF_DEQUANT_Q5_K;
         const int j = 2 * kk;
-        const float d = __half2float(*reinterpret_cast<const __half *>(rp));
+        const __half2 d2 = __half2half2(*reinterpret_cast<const __half *>(rp));
         const float dmin = __half2float(*reinterpret_cast<const __half *>(rp + 2));
         int sc0, mn0, sc1, mn1;
         scale_min_k4(j, rp + 4, sc0, mn0);
         scale_min_k4(j + 1, rp + 4, sc1, mn1);
-        const float dd[2] = {d * (float)sc0, d * (float)sc1}, mm[2] = {dmin * (float)mn0, dmin * (float)mn1};
+        // Half2 form (as convert32): q * sc exact, then one fma with d and
+        // -fp16(dmin * m).
+        const __half2 sc2[2] = {__float2half2_rn((float)sc0), __float2half2_rn((float)sc1)};
+        const __half2 sco[2] = {__float2half2_rn(-1024.0f * (float)sc0), __float2half2_rn(-1024.0f * (float)sc1)};
+        const __half2 mm2[2] = {__float2half2_rn(-dmin * (float)mn0), __float2half2_rn(-dmin * (float)mn1)};
         const uint2 q = *reinterpret_cast<const uint2 *>(rp + (Q5 ? 48 : 16) + 32 * kk + 8 * cp);
         uint2 h = make_uint2(0u, 0u);
         if constexpr (Q5) h = *reinterpret_cast<const uint2 *>(rp + 16 + 8 * cp);
@@ -195,16 +199,9 @@ __device__ __forceinline__ void convert16(const uint8_t *rp, int kk, int cp, uin
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
                 const uint32_t c = qw[i] | hw[i];
-                float f[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    // 2^23 + code, exact; dd*q is exact in fp32, so the fma
-                    // equals the shader's multiply-then-subtract.
-                    const float qf = __uint_as_float(0x4B000000u | ((c >> (8 * e)) & 0xFFu)) - 8388608.0f;
-                    f[e] = fmaf(dd[half], qf, -mm[half]);
-                }
-                o[4 * half + 2 * i] = h2u(__floats2half2_rn(f[0], f[1]));
-                o[4 * half + 2 * i + 1] = h2u(__floats2half2_rn(f[2], f[3]));
+                const uint32_t p0 = __byte_perm(c, 0x64646464u, 0x5140), p1 = __byte_perm(c, 0x64646464u, 0x7362);
+                o[4 * half + 2 * i] = h2u(__hfma2(__hfma2(u2h(p0), sc2[half], sco[half]), d2, mm2[half]));
+                o[4 * half + 2 * i + 1] = h2u(__hfma2(__hfma2(u2h(p1), sc2[half], sco[half]), d2, mm2[half]));
             }
         }
         ca = cp;
@@ -273,9 +270,15 @@ __device__ __forceinline__ void convert32(const uint8_t *rp, uint32_t (&o)[16]) 
             sc = (sb(B + 4) & 0xF) | ((sb(B - 4) >> 6) << 4);
             mn = (sb(B + 4) >> 4) | ((sb(B) >> 6) << 4);
         }
-        const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFF)));
+        // Half2 form: (1024 + q) * sc - 1024 * sc = q * sc exactly (an
+        // integer < 2048; 1024 * sc <= 64512 is exact too), then one fma
+        // with d and -fp16(dmin * m): the weight rounded once, plus the fp16
+        // rounding of the min term (<= 2^-12 * 0.63 absolute at this
+        // format's largest dmin * m).
+        const __half2 d2 = __half2half2(__ushort_as_half((unsigned short)(hd.x & 0xFFFF)));
         const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
-        const float dd = d * (float)sc, mm = dmin * (float)mn;  // exact products
+        const __half2 sc2 = __float2half2_rn((float)sc), sco = __float2half2_rn(-1024.0f * (float)sc);
+        const __half2 mm2 = __float2half2_rn(-dmin * (float)mn);
         constexpr int QO = (Q5 ? 48 : 16) + 32 * (B / 2);
         const uint4 q0 = *reinterpret_cast<const uint4 *>(rp + QO), q1 = *reinterpret_cast<const uint4 *>(rp + QO + 16);
         const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
@@ -289,14 +292,9 @@ __device__ __forceinline__ void convert32(const uint8_t *rp, uint32_t (&o)[16]) 
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const uint32_t c = ((qw[i] >> (4 * (B & 1))) & 0x0F0F0F0Fu) | hw[i];
-            float f[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float qf = __uint_as_float(0x4B000000u | ((c >> (8 * e)) & 0xFFu)) - 8388608.0f;
-                f[e] = fmaf(dd, qf, -mm);
-            }
-            o[2 * i] = h2u(__floats2half2_rn(f[0], f[1]));
-            o[2 * i + 1] = h2u(__floats2half2_rn(f[2], f[3]));
+            const uint32_t p0 = __byte_perm(c, 0x64646464u, 0x5140), p1 = __byte_perm(c, 0x64646464u, 0x7342);
+            o[2 * i] = h2u(__hfma2(__hfma2(u2h(p0), sc2, sco), d2, mm2));
+            o[2 * i + 1] = h2u(__hfma2(__hfma2(u2h(p1), sc2, sco), d2, mm2));
         }
     }
 }
@@ -681,6 +679,9 @@ __global__ void __launch_bounds__(NT, 1)
                         // and columns are clipped by the store).  Every
                         // epilogue thread takes part in every barrier.
                         if (mc >= p.M) continue;  // uniform across the epilogue warps
+#ifdef VKF_QGEMM_NOY
+                        continue;
+#endif
                         auto stage_store = [&](auto sr_c) {
                             constexpr int SR = decltype(sr_c)::value;
 #pragma unroll
@@ -763,10 +764,15 @@ struct Cfg {
 #ifndef VKF_QGEMM_NSMAX
 #define VKF_QGEMM_NSMAX 4
 #endif
-    // Deepest A/B ring (<= 4) that still leaves two packed stages, then as
-    // many packed stages (<= 6) as fit.
-    static constexpr int NS = (SMEM_CAP - FIXED - 2 * RAW_BYTES) / STAGE >= VKF_QGEMM_NSMAX ? VKF_QGEMM_NSMAX
-                              : (SMEM_CAP - FIXED - 2 * RAW_BYTES) / STAGE;
+#ifndef VKF_QGEMM_RSMIN
+#define VKF_QGEMM_RSMIN 3
+#endif
+    // Deepest A/B ring (<= 4) that still leaves RSMIN packed stages (a
+    // packed stage feeds four K-blocks, and with two the next copy had only
+    // one stage-time, ~1.4 us, to arrive from DRAM), then as many packed
+    // stages (<= 6) as fit.
+    static constexpr int NSF = (SMEM_CAP - FIXED - VKF_QGEMM_RSMIN * RAW_BYTES) / STAGE;
+    static constexpr int NS = NSF >= VKF_QGEMM_NSMAX ? VKF_QGEMM_NSMAX : NSF;
     static constexpr int RS0 = (SMEM_CAP - FIXED - NS * STAGE) / RAW_BYTES;
     static constexpr int RS = RS0 > 6 ? 6 : RS0;
     static constexpr size_t SMEM = (size_t)NS * STAGE + (size_t)RS * RAW_BYTES + FIXED;
