@@ -80,3 +80,28 @@ def test_quantize_q8_1_bit_exact(rt):
     yd = G.empty(exp.size)
     rt.quantize_q8_1(xd.data_ptr(), yd.data_ptr(), 7, 512, 512)
     assert np.array_equal(G.host(yd, np.uint8), exp.ravel())
+
+
+def test_quantize_q8_1_ties_and_config4_size(rt):
+    """Quotients exactly on and next to half-integers (where a reciprocal
+    product could round differently from the IEEE division), several scale
+    regimes, and the config 4 activation size: bit-exact with the oracle."""
+    M, K = 512, 5120
+    x = S.normal_f32((M, K), seed=21)
+    # row 0: amax 127 -> d = 1 exactly; values k + 0.5 are ties for roundf
+    x[0, :] = np.resize(np.arange(-126.5, 127.0, 1.0, dtype=np.float32), K)
+    x[0, ::32] = 127.0
+    # row 1: amax 254 -> d = 2; values 2k + 1 are ties
+    x[1, :] = np.resize(np.arange(-253.0, 254.0, 2.0, dtype=np.float32), K)
+    x[1, ::32] = 254.0
+    # row 2: ties one ulp either side
+    t = np.resize(np.arange(-120.5, 121.0, 1.0, dtype=np.float32), K)
+    x[2, :] = np.where(np.arange(K) % 2 == 0, np.nextafter(t, np.float32(np.inf)), np.nextafter(t, np.float32(-np.inf)))
+    x[2, ::32] = 127.0
+    x[3:8] *= np.float32(1e-3)
+    x[8:12] *= np.float32(3e4)
+    exp = po.quantize_q8_1(x)
+    xd = G.dev(x)
+    yd = G.empty(exp.size)
+    rt.quantize_q8_1(xd.data_ptr(), yd.data_ptr(), M, K, K)
+    assert np.array_equal(G.host(yd, np.uint8), exp.ravel())

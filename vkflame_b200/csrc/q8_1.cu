@@ -45,13 +45,19 @@ __global__ void __launch_bounds__(256) quantize_q8_1_kernel(const float *__restr
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     const float d = __fdiv_rn(amax, 127.0f);
+    // v * rn(1/d) is within 2^-23 relative (|v/d| <= 127: 1.6e-5 absolute) of
+    // v / d, so it rounds to the same integer unless the quotient lies that
+    // close to a half-integer; those take the IEEE division.
+    const float r = d != 0.0f ? __frcp_rn(d) : 0.0f;
     int sum = 0;
     uint32_t w[2] = {0u, 0u};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         int q = 0;
         if (d != 0.0f) {
-            q = (int)roundf(__fdiv_rn(v[i], d));
+            float t = v[i] * r;
+            if (fabsf(fabsf(t - truncf(t)) - 0.5f) < 6.2e-5f) t = __fdiv_rn(v[i], d);
+            q = (int)roundf(t);
             q = max(-127, min(127, q));
         }
         sum += q;
