@@ -208,36 +208,60 @@ def stack_groups():
 
 class Stack:
     """One rank's column shard of the stack, run as a CUDA graph of GEMV
-    launches (vkflame_quant_linear_ex) and NCCL all-gathers."""
+    launches.  N = 1: vkflame_quant_linear_ex.  N > 1: each linear is
+    vkflame_quant_linear_gather, the decode GEMV fused with the all-gather
+    (every rank stores its output slice into all ranks' gathered buffers over
+    NVLink as {fp16 pair, epoch} words), and each linear's X is an earlier
+    linear's gathered output (the layer's data flow: qk and the previous down output
+    feed the next layer, o reads qk's, gate/up o's, down gate/up's, the head
+    the last down's), so every gather is waited for, word by word, inside the
+    kernel that reads it.  No NCCL call in the timed region."""
 
     def __init__(self, world, rank, dist, stream):
         import torch
         from vkflame_b200 import rt, shard
         self.rt, self.world, self.rank, self.dist, self.stream = rt, world, rank, dist, stream
-        self.linears = []  # (qtype, K, Nshard, weight, input tensor, output shard, gathered output)
+        self.linears = []  # (qtype, K, Nshard, weight, input tensor, output, gather struct or None)
         self.x_h = torch.randn((1, HIDDEN), device="cuda").half()
         self.x_f = torch.randn((1, FFN), device="cuda").half()
         self.weight_bytes = 0
+        self.gg = None
+        if world > 1:
+            from vkflame_b200.gather import GatherGroup
+            self.gg = GatherGroup(dist, world, rank)
         seed = 1000 * rank
         groups = [g for _ in range(LAYERS) for g in stack_groups()] + [("head", S.Q6_K, HIDDEN, VOCAB, "h")]
-        for name, q, K, N, inp in groups:
+        prev = []  # gathered outputs so far, newest last
+        for i, (name, q, K, N, inp) in enumerate(groups):
             r0, r1 = shard.row_range(N, world, rank)  # this rank's output rows (vkflame_b200/shard.py)
             n = r1 - r0
             seed += 1
             w = make_quant_weight_gpu(q, n, K, seed)
-            y = torch.empty((1, n), device="cuda", dtype=torch.float16)
-            yg = torch.empty((world, 1, n), device="cuda", dtype=torch.float16) if world > 1 else None
-            self.linears.append((q, K, n, w, self.x_h if inp == "h" else self.x_f, y, yg))
+            if world > 1:
+                y = self.gg.buffer(N)
+                src = next((t for t in reversed(prev) if t.N >= K), None)
+                g = self.gg.op(y, x=src)
+                x = src.tensor if src is not None else (self.x_h if inp == "h" else self.x_f)
+                prev.append(y)
+            else:
+                y = torch.empty((1, n), device="cuda", dtype=torch.float16)
+                x, g = (self.x_h if inp == "h" else self.x_f), None
+            self.linears.append((q, K, n, w, x, y, g))
             self.weight_bytes += w.numel()
-        self.out = self.linears[-1][6] if world > 1 else self.linears[-1][5]
+        self.out = self.linears[-1][5] if world == 1 else self.linears[-1][5].tensor
+        torch.cuda.synchronize()
+        barrier(dist)  # every rank's counters initialised before any kernel signals
 
     def step(self):
         rt = self.rt
-        for q, K, n, w, x, y, yg in self.linears:
-            rt.quant_linear_ex(w.data_ptr(), q, x.data_ptr(), rt.X_F16, y.data_ptr(), rt.Y_F16, 1, n, K, K, n,
-                               rt.FLAG_STATIC_WEIGHTS, self.stream)
-            if yg is not None:
-                self.dist.all_gather_into_tensor(yg, y)
+        for q, K, n, w, x, y, g in self.linears:
+            if g is None:
+                rt.quant_linear_ex(w.data_ptr(), q, x.data_ptr(), rt.X_F16, y.data_ptr(), rt.Y_F16, 1, n, K, K, n,
+                                   rt.FLAG_STATIC_WEIGHTS, self.stream)
+            else:
+                ldx = x.shape[2] * 2 if g.x_gathered else x.shape[1]  # gathered X: words of 2 values
+                rt.quant_linear_gather(w.data_ptr(), q, x.data_ptr(), rt.Y_F16, 1, n, K, ldx, y.N,
+                                       rt.FLAG_STATIC_WEIGHTS, g, self.stream)
 
 
 def timed_graph(graph, stream, steps):
@@ -279,7 +303,8 @@ def bench_stack(args, world, rank, local, dist):
         # End to end through the public API with host buffers: pinned token
         # activations -> device, the stack, output-head logits -> pinned host.
         xh = torch.randn((1, HIDDEN)).half().pin_memory()
-        outh = torch.empty(st.out.shape, dtype=torch.float16).pin_memory()
+        # N > 1: the head's gathered buffers ({fp16 pair, epoch} words, both parities)
+        outh = torch.empty(st.out.shape, dtype=st.out.dtype).pin_memory()
         def e2e_step():
             st.x_h.copy_(xh, non_blocking=True)
             g.replay()
@@ -309,7 +334,9 @@ def bench_stack(args, world, rank, local, dist):
                    "layers": LAYERS, "hidden": HIDDEN, "ffn": FFN, "vocab": VOCAB,
                    "weight_gb_per_token": total_bytes / 1e9, "column_shards": world,
                    "launches_per_token": launches_per_step,
-                   "collective": "NCCL all_gather of each linear group's output slice" if world > 1 else "none",
+                   "collective": ("all-gather fused into each GEMV: output slices stored into every rank's buffer over "
+                                  "NVLink (CUDA IPC peer memory) as {fp16 pair, epoch} words, waited for word by word "
+                                  "in the kernel that reads them") if world > 1 else "none",
                    "l2": "weights (9.0 GB) exceed L2; no flush needed"},
         "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks.get("hbm_gbs") else "fallback",
@@ -319,7 +346,7 @@ def bench_stack(args, world, rank, local, dist):
                              "bytes per launch, from the ncu captures of the same kernel on the stack's shapes "
                              "(ratio to algorithmic bytes, profiles/gemv_*.md)"},
         "e2e": {"value": total_bytes / (ems * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": HIDDEN * 2,
-                "d2h_bytes_per_step": int(st.out.numel()) * 2, "ms_per_step": ems},
+                "d2h_bytes_per_step": int(st.out.numel()) * st.out.element_size(), "ms_per_step": ems},
         "gpu_launches": launches_per_step * args.steps, "clocks": clocks,
     }
     return line

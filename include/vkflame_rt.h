@@ -116,6 +116,54 @@ int vkflame_quant_linear(const void *W, int wtype, const void *X, int xtype, voi
 int vkflame_quant_linear_ex(const void *W, int wtype, const void *X, int xtype, void *Y, int ytype,
                             int M, int N, int K, int64_t ldx, int64_t ldy, unsigned flags, void *stream);
 
+/* ---- column-sharded multi-GPU: decode GEMV fused with the all-gather ----
+ * No counterpart in the reference (its runtime is single-device).  The
+ * multi-GPU form of the quantised linear: each rank owns a contiguous range
+ * of output rows (columns of Y), computes its slice with the decode GEMV and
+ * stores it straight into every rank's gathered buffer over NVLink (peer
+ * memory mapped with vkflame_ipc_open): no separate collective launch, no
+ * fence and no completion signal.
+ *
+ * Gathered buffer layout (M = 1, fp16): two buffers per rank, `stride` bytes
+ * apart; buffer (epoch & 1) holds N / 2 words of 8 bytes, word j =
+ * {fp16 Y[2j], fp16 Y[2j + 1], uint32 epoch}.  An aligned 8-byte store is
+ * single-copy atomic, so a reader that sees the epoch sees the data.  A call
+ * with x_gathered reads X from such a buffer and waits (bounded, inside its
+ * kernel) until every word it reads carries its epoch.  epoch is the call
+ * site's run count on the device: run t writes words carrying t + 1 and
+ * expects t + 1 in the words it reads (every call site runs once per step),
+ * and its kernel increments the count when it ends.  Two buffers by parity
+ * let a rank run up to one step ahead without overwriting words a slower
+ * rank has yet to read, which holds when every step reads at least one
+ * gathered X.  One process per GPU; ranks make the same calls in the same
+ * order; buffers and counters zeroed on every rank before the first call
+ * (host barrier).                                                          */
+#define VKF_MAX_RANKS 8
+typedef struct vkf_gather {
+    int world;                       /* ranks, 1 .. VKF_MAX_RANKS                          */
+    int rank;                        /* this rank                                           */
+    void *y_rank[VKF_MAX_RANKS];     /* each rank's buffer 0 (mapped here), at this rank's first word */
+    int64_t stride;                  /* bytes from a rank's buffer 0 to its buffer 1        */
+    int *epoch;                      /* this call site's run count (device int, zero)      */
+    int *done;                       /* this rank's CTA counter (device int, zero)          */
+    int x_gathered;                  /* X is this rank's buffer 0 of an earlier gather      */
+    int64_t x_stride;                /* its bytes from buffer 0 to buffer 1                 */
+} vkf_gather_t;
+
+/* Y slice computed by this rank: rows [0, N) of W (this rank's shard),
+ * written to every rank's gathered buffers at word offset y_rank.  M = 1,
+ * ytype VKF_Y_F16, N even; ldx: X row stride in elements (for a gathered X,
+ * the gathered row length); ldy unused (one row). */
+int vkflame_quant_linear_gather(const void *W, int wtype, const void *X, int ytype, int M, int N, int K,
+                                int64_t ldx, int64_t ldy, unsigned flags, const vkf_gather_t *g, void *stream);
+
+/* CUDA IPC for the gathered buffers and counters: a 64-byte handle of the
+ * allocation holding dev_ptr plus dev_ptr's byte offset in it; open returns
+ * the allocation's base mapped in this process (add the offset). */
+int vkflame_ipc_handle(const void *dev_ptr, void *handle64, uint64_t *offset);
+int vkflame_ipc_open(const void *handle64, void **base);
+int vkflame_ipc_close(void *base);
+
 /* Allocation-free decode GEMV.  No counterpart in the reference: an addition
  * for callers that must not allocate device memory (code inside an
  * allocator callback, processes whose device memory is fully reserved up

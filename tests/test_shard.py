@@ -78,3 +78,17 @@ def test_join_gathered_layout():
     j = shard.join_gathered(g)
     assert j.shape == (3, 8)
     assert (j[:, :4] == g[0]).all() and (j[:, 4:] == g[1]).all()
+
+
+def test_gathered_word_layout_unpack():
+    """{fp16 pair, epoch} words: buffer epoch & 1 of step `epoch`, values in
+    column order; a word of another step is rejected."""
+    from vkflame_b200.gather import unpack
+    y = np.arange(8, dtype=np.float16).reshape(1, 8) * np.float16(0.5)
+    words = np.zeros((2, 1, 4, 2), np.int32)
+    words[1, 0, :, 0] = y.view(np.int32).reshape(-1)
+    words[1, 0, :, 1] = 3
+    assert np.array_equal(unpack(words, 3).view(np.uint16), y.view(np.uint16))
+    words[1, 0, 2, 1] = 1
+    with pytest.raises(ValueError):
+        unpack(words, 3)

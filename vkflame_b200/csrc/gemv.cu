@@ -92,6 +92,23 @@ struct Args {
     int y_f16;
     int prefetch;      // stream weights before the previous kernel on the stream completes
     int whole_tiles;   // S == 1 and W 16-byte aligned: one copy per row block
+    // Fused all-gather (column-sharded multi-GPU, nranks > 0, M = 1, fp16):
+    // Y goes into every rank's gathered buffer as 8-byte words {two fp16,
+    // epoch} (an aligned 8-byte store is single-copy atomic, so a reader that
+    // sees the epoch sees the data: no fence, no completion signal).  Each
+    // rank keeps two buffers, selected by the step's parity, so a rank that
+    // runs ahead never overwrites words a slower rank has yet to read.
+    // x_ll: X is such a gathered buffer; its loader waits (bounded) for the
+    // current epoch in every word it reads, and needs no dependency wait.
+    // epoch: this call site's run count (the words of its run t carry
+    // t + 1; a consumer expects its own count + 1, every op running once per
+    // step), incremented by the grid's last CTA.  Only this call site's
+    // previous run writes it, so it is read before any dependency wait.
+    int nranks, rank, x_ll;
+    uint8_t *ypeer[8];     // each rank's buffer 0, at this rank's first word
+    int64_t ll_stride;     // bytes from a rank's buffer 0 to its buffer 1
+    int64_t x_stride;      // same for X when x_ll
+    int *epoch, *done;
 #ifdef VKF_GEMV_TIMING
     int launch_id;
 #endif
@@ -109,6 +126,57 @@ __device__ __forceinline__ void consumer_bar() {
 __device__ __forceinline__ void store_y(const Args &a, int m, int n, float v) {
     if (a.y_f16) reinterpret_cast<__half *>(a.Y)[(int64_t)m * a.ldy + n] = __float2half_rn(v);
     else reinterpret_cast<float *>(a.Y)[(int64_t)m * a.ldy + n] = v;
+}
+
+// Gathered store of one 16-row block (M = 1): lane l < 16 holds row n0 + l
+// (valid: inside N); even lanes write the pair (n, n + 1) as one 8-byte word
+// {half2, epoch} to every rank.  All 32 lanes call it.
+__device__ __forceinline__ void gather_store(const Args &a, int ep, int n0, float v, bool valid) {
+    const float vn = __shfl_down_sync(0xffffffffu, v, 1);
+    const int lane = threadIdx.x & 31;
+    if (!valid || (lane & 1)) return;
+    const __half2 h = __floats2half2_rn(v, vn);
+    const uint32_t d = *reinterpret_cast<const uint32_t *>(&h);
+    const int64_t off = (int64_t)(ep & 1) * a.ll_stride + (int64_t)((n0 + lane) >> 1) * 8;
+    for (int q = 0; q < a.nranks; ++q)
+        asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};" ::"l"(a.ypeer[q] + off), "r"(d), "r"(ep)
+                     : "memory");
+}
+
+// 32 fp16 X values (64 bytes) of column m, sub-block sb: plain loads, or
+// from a gathered buffer (16 words {half2, epoch}), waiting (bounded) until
+// every word carries the current epoch.
+__device__ __forceinline__ void load_x64(const Args &a, int ep, int m, int sb, uint4 (&v)[4]) {
+    if (!a.x_ll) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(a.X + (int64_t)m * a.ldx_bytes + sb * 64);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) v[c] = __ldg(src + c);
+        return;
+    }
+    const uint8_t *src = a.X + (int64_t)(ep & 1) * a.x_stride + (int64_t)m * a.ldx_bytes + sb * 128;
+    uint32_t d[16];
+    // All 16 loads in flight at once (one memory latency when the words are
+    // there); re-read the set until every epoch matches.
+    for (uint32_t n = 0;; ++n) {
+        uint32_t e[16];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2)
+            asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(d[i]), "=r"(e[i]), "=r"(d[i + 1]), "=r"(e[i + 1])
+                         : "l"(src + 8 * i)
+                         : "memory");
+        bool all = true;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) all = all && e[i] == (uint32_t)ep;
+        if (all) break;
+        if (n == (1u << 22)) {
+            if (a.err) atomicOr(a.err, VKF_KERR_WAIT_TIMEOUT);
+            break;
+        }
+        __nanosleep(20);
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) v[c] = make_uint4(d[4 * c], d[4 * c + 1], d[4 * c + 2], d[4 * c + 3]);
 }
 
 // Resident activations: one thread per (column, 32-value sub-block) reads the
@@ -185,7 +253,7 @@ __device__ __forceinline__ void quantize_run(const Args &a, const uint4 (&v)[4],
 // SUMS: 0 none; 1 K-quant hi + lo fp16 (min-term MMA); 4 K-quant and 5 Q6_K
 // column forms (integer activations, below).
 template <bool OWN, int SUMS, int NTC>
-__device__ __forceinline__ void load_activations(const Args &a, uint8_t *xs, uint8_t *sums) {
+__device__ __forceinline__ void load_activations(const Args &a, int ep, uint8_t *xs, uint8_t *sums) {
     const int nsb = a.K / 32, jobs = a.M * nsb;
     // Every CTA reads the same activations at the same moment: start each CTA
     // at a different run so the requests spread over the row's L2 lines.
@@ -194,10 +262,8 @@ __device__ __forceinline__ void load_activations(const Args &a, uint8_t *xs, uin
         int j = j0 + rot;
         if (j >= jobs) j -= jobs;
         const int m = j / nsb, sb = j - m * nsb;
-        const uint4 *src = reinterpret_cast<const uint4 *>(a.X + (int64_t)m * a.ldx_bytes + sb * 64);
         uint4 v[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) v[c] = __ldg(src + c);
+        load_x64(a, ep, m, sb, v);
 #ifdef VKF_NOXLOAD  // debug experiment only: constant activations instead of loads
 #pragma unroll
         for (int c = 0; c < 4; ++c) v[c] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
@@ -360,6 +426,7 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
         // published to scratch; its last contributor sums all partials in CTA
         // order.  None of this is on the consumers' path.
         asm volatile("griddepcontrol.wait;" ::: "memory");
+        const int ep = a.nranks ? *a.epoch + 1 : 0;
         const int first_tile = it0 / a.S, last_tile = (it1 - 1) / a.S;
         bool ok = true;
         for (int tb = first_tile, k = 0; tb <= last_tile && it1 > it0; ++tb, ++k) {
@@ -395,7 +462,9 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
             if (lane == 0) mbar_arrive(&freed[sl]);
             const bool whole = tb * a.S >= it0 && (tb + 1) * a.S <= it1;
             if (whole) {
-                if constexpr (COLS) {
+                if (a.nranks) {  // M = 1: lane l < 16 holds row tb * 16 + l in o[0]
+                    gather_store(a, ep, tb * 16, o[0], lane < 16 && tb * 16 + lane < a.N);
+                } else if constexpr (COLS) {
                     if (lane < 16 && tb * 16 + lane < a.N) store_y(a, 0, tb * 16 + lane, o[0]);
                 } else {
 #pragma unroll
@@ -426,6 +495,17 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
                 if (fin) __threadfence();
             }
             if (!__shfl_sync(0xffffffffu, fin, 0)) continue;
+            if (a.nranks) {
+                float v = 0.f;
+                if (lane < 16)
+                    for (int c = c_first; c <= c_last; ++c) {
+                        const int wc = tb == first_item(c, a) / a.S ? 0 : 1;
+                        v += __ldcg(a.ws + ((int64_t)c * 2 + wc) * rows16m + lane);
+                    }
+                gather_store(a, ep, tb * 16, v, lane < 16 && tb * 16 + lane < a.N);
+                if (lane == 0) a.cnt[tb] = 0;
+                continue;
+            }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int rc = lane + 32 * j;
@@ -439,6 +519,15 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
                 if (tb * 16 + r < a.N) store_y(a, col, tb * 16 + r, v);
             }
             if (lane == 0) a.cnt[tb] = 0;
+        }
+        if (a.nranks) {
+            // The grid's last CTA advances this call site's run count (every
+            // CTA read it at its start, before arriving here).
+            __syncwarp();
+            if (lane == 0 && atomicAdd(a.done, 1) == a.G - 1) {
+                *a.done = 0;
+                atomicAdd(a.epoch, 1);
+            }
         }
 #ifdef VKF_GEMV_TIMING
         if (lane == 0 && a.launch_id < 4096) {
@@ -464,7 +553,9 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
         const int m = i / ((a.K * 2 + 127) / 128), l = i - m * ((a.K * 2 + 127) / 128);
         asm volatile("prefetch.global.L2 [%0];" ::"l"(a.X + (int64_t)m * a.ldx_bytes + l * 128));
     }
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // A gathered X is validated word by word (its epochs), so its loader
+    // starts without waiting for the previous kernel on the stream.
+    if (!(a.nranks && a.x_ll)) asm volatile("griddepcontrol.wait;" ::: "memory");
 #ifdef VKF_GEMV_TIMING
     if (lane == 0) VKF_TACC(6, tp0);
     const long long tx0 = clock64();
@@ -477,7 +568,8 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
         g_cta_t[a.launch_id][blockIdx.x][1] = gw;
     }
 #endif
-    load_activations<OWN, SUMS, NTC>(a, xs, sums);
+    const int ep = a.nranks ? *a.epoch + 1 : 0;
+    load_activations<OWN, SUMS, NTC>(a, ep, xs, sums);
     consumer_bar<CW>();
 #ifdef VKF_GEMV_TIMING
     if (threadIdx.x == 0 && a.launch_id < 4096) g_cta_t[a.launch_id][blockIdx.x][2] = gtimer();
@@ -815,13 +907,24 @@ static void fill_args(gemv::Args &a, int wtype, const void *W, const void *X, in
 
 // X: fp16, rows 16-byte aligned (ldx_bytes multiple of 16).  Checked by caller.
 int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void *Y, int y_f16, int64_t ldy, int M,
-                int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap, int prefetch) {
+                int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap, int prefetch,
+                const vkf_gather_t *g) {
     DeviceState *ds = device_state();
     if (!ds) return VKF_ERR_NO_DEVICE;
     gemv::Args a{};
     fill_args(a, wtype, W, X, ldx_bytes, Y, y_f16, ldy, M, N, K);
     a.err = ds->d_error;
     a.prefetch = prefetch;
+    if (g) {
+        a.nranks = g->world;
+        a.rank = g->rank;
+        for (int q = 0; q < g->world; ++q) a.ypeer[q] = (uint8_t *)g->y_rank[q];
+        a.ll_stride = g->stride;
+        a.x_ll = g->x_gathered;
+        a.x_stride = g->x_stride;
+        a.epoch = g->epoch;
+        a.done = g->done;
+    }
     return gemv::dispatch(wtype, a, ds->sm_count, stream, ws, ws_cap, cnt, cnt_cap);
 }
 

@@ -13,7 +13,8 @@
 
 namespace vkf {
 int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void *Y, int y_f16, int64_t ldy, int M,
-                int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap, int prefetch);
+                int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap, int prefetch,
+                const vkf_gather_t *g = nullptr);
 size_t gemv_ws_floats(int sms);
 size_t gemv_counters(int N);
 int gemv_cols_per_launch(int K);
@@ -184,6 +185,46 @@ extern "C" int vkflame_quant_linear_ex(const void *W, int wtype, const void *X, 
         vkf::quant_linear(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, (cudaStream_t)stream, flags));
 }
 
+
+// ---- decode GEMV fused with the column all-gather ---------------------------
+
+namespace vkf {
+
+static int quant_linear_gather(const void *W, int wtype, const void *X, int ytype, int M, int N, int K, int64_t ldx,
+                               int64_t ldy, unsigned flags, const vkf_gather_t *g, cudaStream_t stream) {
+    (void)ldy;
+    if (!gemv_format(wtype) || !g) return VKF_ERR_INVALID;
+    if (g->world < 1 || g->world > VKF_MAX_RANKS || g->rank < 0 || g->rank >= g->world) return VKF_ERR_INVALID;
+    if (M != 1 || N < 2 || N % 2 || K < 1 || ytype != VKF_Y_F16 || ldx < K) return VKF_ERR_INVALID;
+    const int qk = vkf_qtype_block_values(wtype);
+    if (K % qk || K % 32) return VKF_ERR_UNSUPPORTED;
+    const int64_t ldx_bytes = g->x_gathered ? ldx * 4 : ldx * 2;  // gathered: 8-byte words of 2 values
+    if (((uintptr_t)X & 15) || ldx_bytes % 16) return VKF_ERR_BADPTR;
+    if (g->x_gathered && (ldx % 4 || g->x_stride % 16)) return VKF_ERR_BADPTR;
+    for (int q = 0; q < g->world; ++q)
+        if (!g->y_rank[q] || ((uintptr_t)g->y_rank[q] & 7)) return VKF_ERR_BADPTR;
+    if (!g->epoch || !g->done || g->stride % 8) return VKF_ERR_BADPTR;
+    const size_t row_bytes = (size_t)K / qk * vkf_qtype_block_bytes(wtype);
+    if (validate_device_range(W, row_bytes * N)) return VKF_ERR_BADPTR;
+    DeviceState *ds = device_state();
+    if (!ds) return VKF_ERR_NO_DEVICE;
+    const size_t ws_floats = gemv_ws_floats(ds->sm_count);
+    float *ws = (float *)stream_scratch(stream, ws_floats * sizeof(float));
+    const size_t ncnt = gemv_counters(N);
+    int *cnt = stream_counters(stream, ncnt);
+    if (!ws || !cnt) return VKF_ERR_NOMEM;
+    return gemv_launch(wtype, W, X, ldx_bytes, g->y_rank[g->rank], 1, N, M, N, K, stream, ws, ws_floats, cnt, ncnt,
+                       (flags & VKF_FLAG_STATIC_WEIGHTS) ? 1 : 0, g);
+}
+
+}  // namespace vkf
+
+extern "C" int vkflame_quant_linear_gather(const void *W, int wtype, const void *X, int ytype, int M, int N, int K,
+                                           int64_t ldx, int64_t ldy, unsigned flags, const vkf_gather_t *g,
+                                           void *stream) {
+    return vkf::set_status(
+        vkf::quant_linear_gather(W, wtype, X, ytype, M, N, K, ldx, ldy, flags, g, (cudaStream_t)stream));
+}
 
 // ---- linear_int8 and the generic linear dispatcher --------------------------
 

@@ -321,3 +321,42 @@ int vkflame_check_kernel_errors(void) {
 uint64_t vkflame_kernel_launch_count(void) { return g_launches.load(); }
 
 }  // extern "C"
+
+// ---- CUDA IPC of device buffers (multi-GPU gathered outputs and counters) ----
+
+extern "C" int vkflame_ipc_handle(const void *dev_ptr, void *handle64, uint64_t *offset) {
+    if (!dev_ptr || !handle64 || !offset) return vkf::set_status(VKF_ERR_INVALID);
+    // cuMemGetAddressRange through the runtime's driver entry point (the
+    // library does not link libcuda directly).
+    using RangeFn = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
+    static RangeFn range = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        return (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+                q == cudaDriverEntryPointSuccess)
+                   ? reinterpret_cast<RangeFn>(p)
+                   : nullptr;
+    }();
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (!range || range(&base, &size, (CUdeviceptr)dev_ptr) != CUDA_SUCCESS) return vkf::set_status(VKF_ERR_BADPTR);
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, (void *)base) != cudaSuccess) return vkf::set_status(VKF_ERR_CUDA);
+    static_assert(sizeof(h) == 64, "IPC handle size");
+    memcpy(handle64, &h, sizeof(h));
+    *offset = (uint64_t)((CUdeviceptr)dev_ptr - base);
+    return vkf::set_status(VKF_OK);
+}
+
+extern "C" int vkflame_ipc_open(const void *handle64, void **base) {
+    if (!handle64 || !base) return vkf::set_status(VKF_ERR_INVALID);
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    if (cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+        return vkf::set_status(VKF_ERR_CUDA);
+    return vkf::set_status(VKF_OK);
+}
+
+extern "C" int vkflame_ipc_close(void *base) {
+    return vkf::set_status(cudaIpcCloseMemHandle(base) == cudaSuccess ? VKF_OK : VKF_ERR_CUDA);
+}

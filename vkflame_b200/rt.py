@@ -51,6 +51,11 @@ _SIGS = {
                                       C.c_int, C.c_int64, C.c_int64, C.c_void_p], C.c_int),
     "vkflame_quantize_q8_1": ([C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int64, C.c_void_p], C.c_int),
     "vkflame_linear_int8": ([C.c_void_p] * 7 + [C.c_int] * 4 + [C.c_void_p], C.c_int),
+    "vkflame_quant_linear_gather": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                     C.c_int64, C.c_int64, C.c_uint, C.c_void_p, C.c_void_p], C.c_int),
+    "vkflame_ipc_handle": ([C.c_void_p, C.c_void_p, C.POINTER(C.c_uint64)], C.c_int),
+    "vkflame_ipc_open": ([C.c_void_p, C.POINTER(C.c_void_p)], C.c_int),
+    "vkflame_ipc_close": ([C.c_void_p], C.c_int),
     "vkflame_get_last_error": ([], C.c_int),
     "vkflame_status_string": ([C.c_int], C.c_char_p),
     "vkflame_check_kernel_errors": ([], C.c_int),
@@ -131,6 +136,40 @@ def dispatch_linear(A: int, B: int, C_: int, D: int, M: int, N: int, K: int, dty
     b = C.byref(C.c_float(beta)) if beta is not None else None
     _check(lib().vkflame_dispatch_linear(None, A, B, C_, D, M, N, K, dtype, transA, transB, act, a, b, stream),
            "dispatch_linear")
+
+
+MAX_RANKS = 8
+
+
+class Gather(C.Structure):
+    """vkf_gather_t (include/vkflame_rt.h)."""
+    _fields_ = [("world", C.c_int), ("rank", C.c_int), ("y_rank", C.c_void_p * MAX_RANKS),
+                ("stride", C.c_int64), ("epoch", C.c_void_p), ("done", C.c_void_p),
+                ("x_gathered", C.c_int), ("x_stride", C.c_int64)]
+
+
+def quant_linear_gather(W: int, wtype: int, X: int, ytype: int, M: int, N: int, K: int, ldx: int, ldy: int,
+                        flags: int, g: Gather, stream: int = 0) -> None:
+    _check(lib().vkflame_quant_linear_gather(W, wtype, X, ytype, M, N, K, ldx, ldy, flags, C.byref(g), stream),
+           "quant_linear_gather")
+
+
+def ipc_handle(ptr: int) -> tuple[bytes, int]:
+    h = (C.c_uint8 * 64)()
+    off = C.c_uint64()
+    _check(lib().vkflame_ipc_handle(ptr, h, C.byref(off)), "ipc_handle")
+    return bytes(h), off.value
+
+
+def ipc_open(handle: bytes) -> int:
+    h = (C.c_uint8 * 64).from_buffer_copy(handle)
+    base = C.c_void_p()
+    _check(lib().vkflame_ipc_open(h, C.byref(base)), "ipc_open")
+    return base.value
+
+
+def ipc_close(base: int) -> None:
+    _check(lib().vkflame_ipc_close(base), "ipc_close")
 
 
 def check_kernel_errors() -> None:
