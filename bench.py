@@ -334,7 +334,9 @@ def bench_stack(args, world, rank, local, dist):
                    "layers": LAYERS, "hidden": HIDDEN, "ffn": FFN, "vocab": VOCAB,
                    "weight_gb_per_token": total_bytes / 1e9, "column_shards": world,
                    "launches_per_token": launches_per_step,
-                   "collective": ("all-gather fused into each GEMV: output slices stored into every rank's buffer over "
+                   "dataflow": ("chained: each linear reads an earlier linear's gathered output" if world > 1
+                             else "independent: each linear reads its layer input"),
+                "collective": ("all-gather fused into each GEMV: output slices stored into every rank's buffer over "
                                   "NVLink (CUDA IPC peer memory) as {fp16 pair, epoch} words, waited for word by word "
                                   "in the kernel that reads them") if world > 1 else "none",
                    "l2": "weights (9.0 GB) exceed L2; no flush needed"},
