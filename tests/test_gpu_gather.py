@@ -19,6 +19,13 @@ from vkflame_b200 import synth as S
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(scope="module")
+def rt():
+    from vkflame_b200 import rt as _rt
+    _rt.lib()
+    return _rt
+
 KA, NA, KB, NB = 1024, 512, 512, 256   # linear A: Q4_K 1024 -> 512; linear B: Q8_0 512 -> 256 (X = A's output)
 STEPS = 3
 
@@ -85,3 +92,49 @@ def test_quant_linear_gather_two_ranks():
     assert G.normwise_err(ya[0].astype(np.float64), ref_a) < G.REL_TOL
     ref_b = ya[0].astype(np.float64)[:, :KB] @ wb.astype(np.float64).T
     assert G.normwise_err(yb[0].astype(np.float64), ref_b) < G.REL_TOL
+
+
+def test_quant_linear_gather_world1_matches_gemv_bitwise(rt):
+    """World size 1 (no peers): the gathered words hold exactly the plain
+    GEMV's fp16 outputs, over two runs (both buffer parities), with the
+    second linear reading the first's gathered output."""
+    import torch
+    from vkflame_b200.gather import GatherGroup, unpack
+    wa = G.dev(S.quant_matrix(S.Q4_K, NA, KA, seed=5))
+    wb = G.dev(S.quant_matrix(S.Q6_K, NB, KB, seed=8))
+    x = G.dev(S.normal_f16((1, KA), seed=7))
+    gg = GatherGroup(None, 1, 0)
+    ya, yb = gg.buffer(NA), gg.buffer(NB)
+    ga, gb = gg.op(ya), gg.op(yb, x=ya)
+    for step in (1, 2):
+        rt.quant_linear_gather(wa.data_ptr(), S.Q4_K, x.data_ptr(), rt.Y_F16, 1, NA, KA, KA, NA, 0, ga)
+        rt.quant_linear_gather(wb.data_ptr(), S.Q6_K, ya.tensor.data_ptr(), rt.Y_F16, 1, NB, KB, NA, NB, 0, gb)
+        torch.cuda.synchronize()
+        rt.check_kernel_errors()
+        a = unpack(ya.tensor.cpu().numpy(), step)
+        b = unpack(yb.tensor.cpu().numpy(), step)
+        ref_a = G.empty(NA * 2)
+        rt.quant_linear_ex(wa.data_ptr(), S.Q4_K, x.data_ptr(), rt.X_F16, ref_a.data_ptr(), rt.Y_F16, 1, NA, KA, KA,
+                           NA, 0)
+        xa = torch.from_numpy(a.view(np.int16).copy()).cuda()
+        ref_b = G.empty(NB * 2)
+        rt.quant_linear_ex(wb.data_ptr(), S.Q6_K, xa.data_ptr(), rt.X_F16, ref_b.data_ptr(), rt.Y_F16, 1, NB, KB, NA,
+                           NB, 0)
+        assert np.array_equal(a.view(np.uint16).ravel(), G.host(ref_a, np.uint16))
+        assert np.array_equal(b.view(np.uint16).ravel(), G.host(ref_b, np.uint16))
+
+
+def test_quant_linear_gather_rejects_bad_args(rt):
+    from vkflame_b200.gather import GatherGroup
+    w = G.dev(S.quant_matrix(S.Q4_K, 64, 512, seed=1))
+    x = G.dev(S.normal_f16((2, 512), seed=2))
+    gg = GatherGroup(None, 1, 0)
+    y = gg.buffer(64)
+    g = gg.op(y)
+    bad = [dict(M=2), dict(ytype=rt.Y_F32), dict(N=63), dict(X=x.data_ptr() + 2)]
+    for b in bad:
+        a = dict(W=w.data_ptr(), wtype=S.Q4_K, X=x.data_ptr(), ytype=rt.Y_F16, M=1, N=64, K=512, ldx=512, ldy=64)
+        a.update(b)
+        with pytest.raises(rt.VkflameError):
+            rt.quant_linear_gather(a["W"], a["wtype"], a["X"], a["ytype"], a["M"], a["N"], a["K"], a["ldx"], a["ldy"],
+                                   0, g)
