@@ -524,24 +524,15 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
                 for (int i = 0; i < RPL; ++i) {
                     const int r = rows[i];
-#ifndef VKF_QGEMM_NOCONV
                     uint4 va, vb;
                     int ca, cb;
                     convert16<QT>(rt + r * RB, kk, cp, va, vb, ca, cb);
                     uint8_t *rowp = at + (r >> 3) * 1024 + (r & 7) * 128;
-#ifdef VKF_QGEMM_NOSTS
-                    if ((va.x ^ vb.y) == 0x12345678u)  // keep the conversion live
-#endif
-                    {
-                        *reinterpret_cast<uint4 *>(rowp + ((ca ^ (r & 7)) << 4)) = va;
-                        *reinterpret_cast<uint4 *>(rowp + ((cb ^ (r & 7)) << 4)) = vb;
-                    }
-#endif
+                    *reinterpret_cast<uint4 *>(rowp + ((ca ^ (r & 7)) << 4)) = va;
+                    *reinterpret_cast<uint4 *>(rowp + ((cb ^ (r & 7)) << 4)) = vb;
                 }
                 // generic-proxy stores -> visible to the tensor core's async proxy
-#ifndef VKF_QGEMM_NOFENCE
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-#endif
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&ab_full[s]);
                 QT_ACC(2);
@@ -679,9 +670,6 @@ __global__ void __launch_bounds__(NT, 1)
                         // and columns are clipped by the store).  Every
                         // epilogue thread takes part in every barrier.
                         if (mc >= p.M) continue;  // uniform across the epilogue warps
-#ifdef VKF_QGEMM_NOY
-                        continue;
-#endif
                         auto stage_store = [&](auto sr_c) {
                             constexpr int SR = decltype(sr_c)::value;
 #pragma unroll
@@ -710,9 +698,6 @@ __global__ void __launch_bounds__(NT, 1)
                     }
                     if (!ok || n >= p.N || mc >= p.M) continue;
                     const int nm = min(32, p.M - mc);
-#ifdef VKF_QGEMM_NOY
-                    if (v[0] == 1234.5f && v[31] == -1.f)
-#endif
                     if (p.y_f16) {
                         __half *yp = reinterpret_cast<__half *>(p.Y) + (int64_t)mc * p.ldy + n;
 #pragma unroll

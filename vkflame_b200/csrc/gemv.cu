@@ -264,10 +264,6 @@ __device__ __forceinline__ void load_activations(const Args &a, int ep, uint8_t 
         const int m = j / nsb, sb = j - m * nsb;
         uint4 v[4];
         load_x64(a, ep, m, sb, v);
-#ifdef VKF_NOXLOAD  // debug experiment only: constant activations instead of loads
-#pragma unroll
-        for (int c = 0; c < 4; ++c) v[c] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
-#endif
         if constexpr (SUMS >= 4) {
             quantize_run<SUMS>(a, v, m, sb, xs, sums);
             continue;
