@@ -67,7 +67,7 @@ constexpr int W_RAW = 6, W_CONV = 7;
 constexpr int NT = 32 * (W_CONV + CV);
 constexpr int A_BYTES = BW * 128;
 constexpr int SMEM_CAP = 232448;
-constexpr int EPI_BUF = 4096;  // one Y staging buffer: 16 rows fp16 / 8 rows fp32 of 128 columns
+constexpr int EPI_BUF = 16384;  // one Y staging buffer: 32 rows (one TMEM chunk) of 128 fp32 columns
 
 // Packed bytes of one row's 256 values.
 template <int QT>
@@ -665,7 +665,7 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + v[j];
                     if (p.y_tma) {
-                        // Stage SR rows x 128 columns in shared memory and
+                        // Stage the chunk's 32 rows x 128 columns in shared memory and
                         // write them with one tensor store (out-of-range rows
                         // and columns are clipped by the store).  Every
                         // epilogue thread takes part in every barrier.
@@ -679,7 +679,7 @@ __global__ void __launch_bounds__(NT, 1)
                                 epi_bar();
 #pragma unroll
                                 for (int i = 0; i < SR; ++i) {
-                                    if constexpr (SR == 16)
+                                    if (p.y_f16)
                                         reinterpret_cast<__half *>(buf)[i * BW + nl] = __float2half_rn(v[sub + i]);
                                     else
                                         reinterpret_cast<float *>(buf)[i * BW + nl] = v[sub + i];
@@ -692,8 +692,7 @@ __global__ void __launch_bounds__(NT, 1)
                                 }
                             }
                         };
-                        if (p.y_f16) stage_store(std::integral_constant<int, 16>{});
-                        else stage_store(std::integral_constant<int, 8>{});
+                        stage_store(std::integral_constant<int, 32>{});
                         continue;
                     }
                     if (!ok || n >= p.N || mc >= p.M) continue;
@@ -750,12 +749,11 @@ struct Cfg {
 #define VKF_QGEMM_NSMAX 4
 #endif
 #ifndef VKF_QGEMM_RSMIN
-#define VKF_QGEMM_RSMIN 3
+#define VKF_QGEMM_RSMIN 2
 #endif
     // Deepest A/B ring (<= 4) that still leaves RSMIN packed stages (a
-    // packed stage feeds four K-blocks, and with two the next copy had only
-    // one stage-time, ~1.4 us, to arrive from DRAM), then as many packed
-    // stages (<= 6) as fit.
+    // packed stage feeds four K-blocks; three instead of two measured no
+    // different), then as many packed stages (<= 6) as fit.
     static constexpr int NSF = (SMEM_CAP - FIXED - VKF_QGEMM_RSMIN * RAW_BYTES) / STAGE;
     static constexpr int NS = NSF >= VKF_QGEMM_NSMAX ? VKF_QGEMM_NSMAX : NSF;
     static constexpr int RS0 = (SMEM_CAP - FIXED - NS * STAGE) / RAW_BYTES;
@@ -765,13 +763,13 @@ struct Cfg {
     static constexpr bool FITS = NS >= 2 && RS >= 2 && (!ATM || (NB * BX + NS * 32 <= 512 && CV == 8));
 };
 
-// Columns per tile (NB x BX) for M activation rows; mirrors launch_q.  Up
-// to 256 the converted weight tile lives in TMEM (no shared-memory traffic
-// for it); above 256, where the 512-column accumulator leaves no TMEM for
-// it, the shared-memory form with one weight decode per 512 activation rows
-// is faster (Q4_K 5120 x 13824, M = 512: 86 against 106 us for two 256-row
-// tiles in the TMEM form), except Q8_0, whose packed stages leave no room
-// for a 512-column ring.
+// Columns per tile (NB x BX) for M activation rows; mirrors launch_q.  The
+// converted weight tile lives in TMEM (tiles of up to 256 activation rows;
+// more rows take several tiles, each decoding the weights again, which the
+// half2 conversion makes cheap: Q4_K 5120 x 13824, M = 512, 70 us against 83
+// us for the shared-memory form with one 512-column tile).  The 512-column
+// shared-memory form is kept for builds with VKF_QGEMM_ATM=0 where its ring
+// fits.
 template <int QT>
 static int tile_cols(int M) {
     if constexpr (Cfg<QT, 256, 2, false>::FITS) {
@@ -811,11 +809,11 @@ static int launch(const void *W, const void *X, int64_t ldx, void *Y, int y_f16,
     const int grid = grid_for(units);
     int *flags = stream_counters(stream, (size_t)grid);
     if (!flags) return VKF_ERR_NOMEM;
-    // Y rows 16-byte aligned: tensor stores of 16 (fp16) or 8 (fp32) rows x 128 columns
+    // Y rows 16-byte aligned: tensor stores of 32 rows (one TMEM chunk) x 128 columns
     CUtensorMap ty;
     memset(&ty, 0, sizeof(ty));
     const int esize = y_f16 ? 2 : 4;
-    const int y_tma = make_rowmajor_map(&ty, Y, esize, M, N, ldy, BW, EPI_BUF / (BW * esize)) ? 1 : 0;
+    const int y_tma = make_rowmajor_map(&ty, Y, esize, M, N, ldy, BW, 32) ? 1 : 0;
     Params p{M, N, K, Y, ldy, y_f16, y_tma, prefetch, units, ws, flags, ds->d_error};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
