@@ -92,3 +92,63 @@ def test_gathered_word_layout_unpack():
     words[1, 0, 2, 1] = 1
     with pytest.raises(ValueError):
         unpack(words, 3)
+
+
+def _gather_group_main(rank, world, port, out):
+    """Host side of the NVLink gather set-up on gloo (CPU tensors, fake IPC):
+    handle exchange order, one mapping per peer allocation, word offsets of
+    each rank's slice, parity strides, per-call-site counters."""
+    import torch
+    import torch.distributed as dist
+    from vkflame_b200 import gather, rt
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    opened = []
+    # fake IPC: a handle names (rank, allocation base); "opening" maps rank
+    # q's allocation to 10**12 * (q + 1) + its base in this process
+    rt.ipc_handle = lambda ptr: (f"{rank}:{ptr}".encode().ljust(64, b"\0"), 0)
+
+    def fake_open(h):
+        q, base = h.rstrip(b"\0").decode().split(":")
+        opened.append(h)
+        return 10**12 * (int(q) + 1) + int(base)
+    rt.ipc_open = fake_open
+    rt.ipc_close = lambda base: None
+    try:
+        gg = gather.GatherGroup(dist, world, rank, device="cpu")
+        ya, yb = gg.buffer(1024), gg.buffer(256)
+        ga, gb = gg.op(ya), gg.op(yb, x=ya)
+        out.put((rank, [ya.ptrs, yb.ptrs], [ya.tensor.data_ptr(), yb.tensor.data_ptr()],
+                 [list(ga.y_rank)[:world], list(gb.y_rank)[:world]], ga.stride, gb.stride,
+                 ga.x_gathered, gb.x_gathered, gb.x_stride, ga.epoch != gb.epoch, len(opened)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_group_host_logic_two_ranks():
+    world = 2
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_group_main, args=(r, world, port, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r = out.get(timeout=60)
+        res[r[0]] = r
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, (_, ptrs, own, yr, sa, sb, xa, xb, xsb, distinct, nopen) in res.items():
+        peer = 1 - rank
+        for i, (n_full) in enumerate((1024, 256)):
+            assert ptrs[i][rank] == own[i]                                   # own buffer, unmapped
+            assert ptrs[i][peer] == 10**12 * (peer + 1) + res[peer][2][i]    # the peer's buffer, mapped
+            r0 = shard.row_range(n_full, world, rank)[0]
+            assert yr[i] == [p + (r0 // 2) * 8 for p in ptrs[i]]             # this rank's first word everywhere
+        assert (sa, sb) == (1024 // 2 * 8, 256 // 2 * 8)                    # buffer 0 -> buffer 1, one row
+        assert (xa, xb, xsb) == (0, 1, 1024 // 2 * 8)
+        assert distinct                                                      # one run counter per call site
+        assert nopen == 2                                                    # each peer allocation opened once

@@ -36,12 +36,12 @@ class GatherGroup:
     must pass a host barrier after the last call and before the first
     gathered launch (buffers are zero, epochs 0)."""
 
-    def __init__(self, dist, world: int, rank: int):
+    def __init__(self, dist, world: int, rank: int, device: str = "cuda"):
         import torch
         if not 1 <= world <= rt.MAX_RANKS:
             raise ValueError(f"world {world} outside 1..{rt.MAX_RANKS}")
-        self.dist, self.world, self.rank = dist, world, rank
-        self.done = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.dist, self.world, self.rank, self.device = dist, world, rank, device
+        self.done = torch.zeros(1, dtype=torch.int32, device=device)
         self.epochs = []  # one run counter per call site (op)
         self._opened: dict[bytes, int] = {}
 
@@ -67,7 +67,7 @@ class GatherGroup:
         import torch
         if N % (2 * self.world):
             raise ValueError(f"N = {N} must split into even slices over {self.world} ranks")
-        t = torch.zeros((2, M, N // 2, 2), dtype=torch.int32, device="cuda")
+        t = torch.zeros((2, M, N // 2, 2), dtype=torch.int32, device=self.device)
         return GatheredBuffer(t, self._share(t.data_ptr()), N, M)
 
     def op(self, out: GatheredBuffer, x: GatheredBuffer | None = None) -> "rt.Gather":
@@ -75,7 +75,7 @@ class GatherGroup:
         reading X from the gathered buffer `x` (None: X is an ordinary fp16
         row).  Every call site must run once per step."""
         import torch
-        ep = torch.zeros(1, dtype=torch.int32, device="cuda")
+        ep = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.epochs.append(ep)
         r0, _ = shard.row_range(out.N, self.world, self.rank)
         g = rt.Gather()
