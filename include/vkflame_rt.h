@@ -174,7 +174,11 @@ int vkflame_ipc_close(void *base);
  * and it never calls cudaMalloc/cudaFree.
  *   Limits: 1 <= M <= 8, N <= 262144, M * (2K + 160 + K/8) <= 80 KiB,
  *   X rows 16-byte aligned; anything else returns VKF_ERR_INVALID,
- *   VKF_ERR_UNSUPPORTED or VKF_ERR_BADPTR and launches nothing.
+ *   VKF_ERR_UNSUPPORTED or VKF_ERR_BADPTR and queues nothing on the stream.
+ *   W, X and Y get alignment checks only: their ranges are not validated.
+ * A bounded wait that gives up inside its kernel is reported, like every
+ * other kernel's, by vkflame_check_kernel_errors (which allocates nothing
+ * when only this entry point has run on the device).
  * The first call on a device looks up the scratch's device address
  * (cudaGetSymbolAddress); make that call before any stream capture.
  * Every call shares the one scratch array: calls whose kernels may overlap
@@ -205,7 +209,8 @@ int vkflame_linear_int8(const int8_t *X, const int8_t *W, const float *sx, const
 int vkflame_get_last_error(void);
 const char *vkflame_status_string(int status);
 /* Synchronises the current device and reports (and clears) the error bits
- * kernels set when a bounded wait gave up: VKF_ERR_TIMEOUT if any was set. */
+ * kernels set when a bounded wait gave up: VKF_ERR_TIMEOUT if any was set.
+ * Covers every entry point, the allocation-free one included. */
 int vkflame_check_kernel_errors(void);
 /* Number of kernels this library has launched since load (all devices). */
 uint64_t vkflame_kernel_launch_count(void);

@@ -137,7 +137,8 @@ extern "C" void vkref_{name}(void **bindings, const void *push, unsigned gx, uns
 
 
 def main(reference: str | None = None) -> int:
-    ref = Path(reference or os.environ.get("VKFLAME_REFERENCE", "/root/reference"))
+    # $VKFLAME_REFERENCE, else a "reference" directory beside this repository
+    ref = Path(reference or os.environ.get("VKFLAME_REFERENCE") or Path(__file__).resolve().parents[2] / "reference")
     kdir = ref / "kernels"
     if not kdir.is_dir():
         print(f"[build_ref] reference shaders not found at {kdir}; skipping", file=sys.stderr)

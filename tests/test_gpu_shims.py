@@ -226,6 +226,35 @@ def test_hipblas_hgemm_all_layouts(hip, blas, tA, tB):
     assert np.abs(got - ref).max() / np.abs(ref).max() < 2e-3
 
 
+@pytest.mark.parametrize("m,n,k", [(80, 200, 64), (20000, 64, 128), (64, 20000, 128)])
+def test_hipblas_hgemm_both_operands_staged(hip, blas, m, n, k):
+    """op(A) = A and op(B) = B^T: both operands are copied K-major into the
+    stream's scratch; n > m and m > n (the large cases exceed the arena's
+    minimum size, so an overlap or overrun of the two regions shows)."""
+    rng = np.random.default_rng(m + n)
+    A = rng.standard_normal((m, k)).astype(np.float16)  # op N: m x k, column-major (lda = m)
+    B = rng.standard_normal((n, k)).astype(np.float16)  # op T: stored n x k column-major (ldb = n)
+    Ad, Bd, Cd = Dev(hip, colmajor(A).T.copy()), Dev(hip, colmajor(B).T.copy()), Dev(hip, nbytes=m * n * 2)
+    one, zero = C.c_uint16(int(np.float16(1).view(np.uint16))), C.c_uint16(0)
+    rc = blas.hipblasHgemm(blas.handle, OP_N, OP_T, m, n, k, C.byref(one), C.c_void_p(Ad.ptr), m, C.c_void_p(Bd.ptr),
+                           n, C.byref(zero), C.c_void_p(Cd.ptr), m)
+    assert rc == 0
+    got = Cd.get(np.float16, (n, m)).T.astype(np.float64)
+    ref = A.astype(np.float64) @ B.astype(np.float64).T
+    assert np.abs(got - ref).max() / np.abs(ref).max() < 2e-3
+
+
+def test_hipblas_k_zero_scales_c(hip, blas):
+    """k = 0 is a valid hipBLAS call: C = beta * C."""
+    m, n = 33, 17
+    c0 = np.random.default_rng(9).standard_normal((n, m)).astype(np.float32)
+    Cd = Dev(hip, c0)
+    one, half = C.c_float(1.0), C.c_float(0.5)
+    assert blas.hipblasSgemm(blas.handle, OP_N, OP_N, m, n, 0, C.byref(one), None, m, None, 1, C.byref(half),
+                             C.c_void_p(Cd.ptr), m) == 0
+    assert np.array_equal(Cd.get(np.float32, (n, m)), c0 * np.float32(0.5))
+
+
 def test_hipblas_sgemm_tf32(hip, blas):
     m, n, k = 128, 64, 256
     rng = np.random.default_rng(2)

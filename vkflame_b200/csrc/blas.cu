@@ -31,6 +31,7 @@ int gemm_tf32_tn(const float *A, int64_t lda, const float *B, int64_t ldb, int M
                  int y_f16, cudaStream_t stream);
 int transpose(const void *src, int64_t lds, void *dst, int64_t ldd, int rows, int cols, int esize,
               cudaStream_t stream);
+int scale_c(void *C, int ctype, int64_t ldc, int m, int n, float beta, cudaStream_t stream);
 
 
 static int esize_of(int t) { return t == BT_F16 ? 2 : t == BT_I8 ? 1 : 4; }
@@ -67,13 +68,17 @@ int blas_gemm_ex(int transA, int transB, int m, int n, int k, float alpha, const
     if (m == 0 || n == 0) return VKF_OK;
     if (atype != btype || (atype != BT_F16 && atype != BT_F32 && atype != BT_I8)) return VKF_ERR_UNSUPPORTED;
     if (ctype != BT_F16 && ctype != BT_F32 && !(ctype == BT_I32 && atype == BT_I8)) return VKF_ERR_UNSUPPORTED;
-    if (!A || !B || !C) return VKF_ERR_BADPTR;
-    if (ldc < m || lda < (transA ? k : m) || ldb < (transB ? n : k)) return VKF_ERR_INVALID;
+    if (!C) return VKF_ERR_BADPTR;
+    if (ldc < m) return VKF_ERR_INVALID;
+    if (k == 0) return scale_c(C, ctype, ldc, m, n, beta, stream);  // hipBLAS: C = beta * C
+    if (!A || !B) return VKF_ERR_BADPTR;
+    if (lda < (transA ? k : m) || ldb < (transB ? n : k)) return VKF_ERR_INVALID;
     const int es = esize_of(atype);
     const int64_t kp = ((int64_t)k * es + 15) / 16 * 16 / es;
-    const size_t abytes = ((size_t)m * kp * es + 255) & ~size_t(255);
-    const size_t bbytes = ((size_t)n * kp * es + 255) & ~size_t(255);
-    uint8_t *scr = (uint8_t *)stream_scratch(stream, abytes + bbytes);
+    // Staging regions: A'' (n rows, from B) first, then B'' (m rows, from A).
+    const size_t a2bytes = ((size_t)n * kp * es + 255) & ~size_t(255);
+    const size_t b2bytes = ((size_t)m * kp * es + 255) & ~size_t(255);
+    uint8_t *scr = (uint8_t *)stream_scratch(stream, a2bytes + b2bytes);
     if (!scr) return VKF_ERR_NOMEM;
     // A'' (n x k) from B: K-major iff op(B) = B (column-major k x n = row-major n x k).
     const void *a2, *b2;
@@ -81,9 +86,8 @@ int blas_gemm_ex(int transA, int transB, int m, int n, int k, float alpha, const
     int rc = prepare(B, ldb, n, k, es, !transB, scr, &a2, &lda2, stream);
     if (rc) return rc;
     // B'' (m x k) from A: K-major iff op(A) = A^T (column-major k x m = row-major m x k).
-    rc = prepare(A, lda, m, k, es, transA, scr + abytes, &b2, &ldb2, stream);
+    rc = prepare(A, lda, m, k, es, transA, scr + a2bytes, &b2, &ldb2, stream);
     if (rc) return rc;
-    if (k == 0) return VKF_ERR_UNSUPPORTED;
     const int y_f16 = ctype == BT_F16;
     if (atype == BT_I8) {
         if (alpha != 1.0f || beta != 0.0f) return VKF_ERR_UNSUPPORTED;

@@ -737,8 +737,9 @@ struct Launcher {
 
     // require_whole: plan only (return VKF_ERR_UNSUPPORTED without launching)
     // unless every item is a whole row block with at least two ring stages.
+    // plan_only: every check of a launch, and no launch (VKF_OK if it would launch).
     static int launch(Args &a, int sms, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap,
-                      bool require_whole = false) {
+                      bool require_whole = false, bool plan_only = false) {
         auto up = [](int64_t v, int64_t m) { return (v + m - 1) / m * m; };
         a.units = (a.K + 255) / 256;
         // Column pitches: the owned layout's 16-byte fragment loads want
@@ -789,6 +790,9 @@ struct Launcher {
         a.off_red = a.off_ring + a.nst * a.stage_bytes;
         a.off_bar = a.off_red + red_bytes;
         const size_t smem = (size_t)a.off_bar + bar_bytes;
+        const int grid = std::max(1, std::min(CPS * sms, a.I));
+        if ((size_t)grid * 2 * rows16m > ws_cap || (size_t)a.T > cnt_cap) return VKF_ERR_INVALID;
+        if (plan_only) return VKF_OK;
         static bool attr_set[64] = {false};
         int dev = 0;
         cudaGetDevice(&dev);
@@ -796,8 +800,7 @@ struct Launcher {
             cudaFuncSetAttribute(gemv_kernel<QT, CW, M1, CPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_cap);
             attr_set[dev] = true;
         }
-        a.G = std::max(1, std::min(CPS * sms, a.I));
-        if ((size_t)a.G * 2 * rows16m > ws_cap || (size_t)a.T > cnt_cap) return VKF_ERR_INVALID;
+        a.G = grid;
         a.ws = ws;
         a.cnt = cnt;
         cudaLaunchConfig_t cfg = {};
@@ -830,25 +833,27 @@ constexpr int CW_DEFAULT = 8;
 // its weights, as soon as either CTA of this one finishes (measured ~12 %
 // faster on the 14B stack's Q4_K shapes); otherwise one CTA per SM.
 template <int QT>
-static int launch_q(Args &a, int sms, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap) {
+static int launch_q(Args &a, int sms, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap,
+                    bool plan_only) {
     constexpr bool COLS_FMT = QT == VKF_DEQUANT_Q4_K || QT == VKF_DEQUANT_Q5_K || QT == VKF_DEQUANT_Q6_K;
     if (COLS_FMT && a.M == 1) {
         Args b = a;
-        const int rc = Launcher<QT, CW_DEFAULT, true, 2>::launch(b, sms, stream, ws, ws_cap, cnt, cnt_cap, true);
+        const int rc =
+            Launcher<QT, CW_DEFAULT, true, 2>::launch(b, sms, stream, ws, ws_cap, cnt, cnt_cap, true, plan_only);
         if (rc != VKF_ERR_UNSUPPORTED) return rc;
-        return Launcher<QT, CW_DEFAULT, true, 1>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+        return Launcher<QT, CW_DEFAULT, true, 1>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap, false, plan_only);
     }
-    return Launcher<QT, CW_DEFAULT, false, 1>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    return Launcher<QT, CW_DEFAULT, false, 1>::launch(a, sms, stream, ws, ws_cap, cnt, cnt_cap, false, plan_only);
 }
 
 static int dispatch(int wtype, Args &a, int sms, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt,
-                    size_t cnt_cap) {
+                    size_t cnt_cap, bool plan_only = false) {
     switch (wtype) {
-    case VKF_DEQUANT_Q4_0: return launch_q<VKF_DEQUANT_Q4_0>(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    case VKF_DEQUANT_Q8_0: return launch_q<VKF_DEQUANT_Q8_0>(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    case VKF_DEQUANT_Q4_K: return launch_q<VKF_DEQUANT_Q4_K>(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    case VKF_DEQUANT_Q5_K: return launch_q<VKF_DEQUANT_Q5_K>(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
-    case VKF_DEQUANT_Q6_K: return launch_q<VKF_DEQUANT_Q6_K>(a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    case VKF_DEQUANT_Q4_0: return launch_q<VKF_DEQUANT_Q4_0>(a, sms, stream, ws, ws_cap, cnt, cnt_cap, plan_only);
+    case VKF_DEQUANT_Q8_0: return launch_q<VKF_DEQUANT_Q8_0>(a, sms, stream, ws, ws_cap, cnt, cnt_cap, plan_only);
+    case VKF_DEQUANT_Q4_K: return launch_q<VKF_DEQUANT_Q4_K>(a, sms, stream, ws, ws_cap, cnt, cnt_cap, plan_only);
+    case VKF_DEQUANT_Q5_K: return launch_q<VKF_DEQUANT_Q5_K>(a, sms, stream, ws, ws_cap, cnt, cnt_cap, plan_only);
+    case VKF_DEQUANT_Q6_K: return launch_q<VKF_DEQUANT_Q6_K>(a, sms, stream, ws, ws_cap, cnt, cnt_cap, plan_only);
     default: return VKF_ERR_UNSUPPORTED;
     }
 }
@@ -926,15 +931,15 @@ int gemv_launch(int wtype, const void *W, const void *X, int64_t ldx_bytes, void
 
 // Same launch with the SM count and the kernel error word supplied by the
 // caller, so that nothing here allocates device memory (the allocation-free
-// entry point in noalloc.cu).
+// entry point in noalloc.cu).  plan_only: run every check, launch nothing.
 int gemv_launch_raw(int wtype, const void *W, const void *X, int64_t ldx_bytes, void *Y, int y_f16, int64_t ldy,
                     int M, int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap,
-                    int sms, unsigned *err) {
+                    int sms, unsigned *err, int plan_only) {
     gemv::Args a{};
     fill_args(a, wtype, W, X, ldx_bytes, Y, y_f16, ldy, M, N, K);
     a.err = err;
     a.prefetch = 0;
-    return gemv::dispatch(wtype, a, sms, stream, ws, ws_cap, cnt, cnt_cap);
+    return gemv::dispatch(wtype, a, sms, stream, ws, ws_cap, cnt, cnt_cap, plan_only != 0);
 }
 
 }  // namespace vkf

@@ -4,6 +4,11 @@
 
 #include "rt_internal.h"
 
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <type_traits>
+
 namespace vkf {
 namespace {
 
@@ -25,7 +30,36 @@ __global__ void __launch_bounds__(256) transpose_kernel(const T *__restrict__ sr
     }
 }
 
+// C[j * ldc + i] = beta * C[j * ldc + i] for i < m, j < n (column-major);
+// beta == 0 writes zeros without reading C (BLAS convention: NaNs in C do
+// not propagate).
+template <typename T>
+__global__ void __launch_bounds__(256) scale_kernel(T *C, int64_t ldc, int m, int n, float beta) {
+    const int64_t total = (int64_t)m * n;
+    for (int64_t e = blockIdx.x * 256ll + threadIdx.x; e < total; e += (int64_t)gridDim.x * 256) {
+        const int64_t j = e / m, i = e - j * m;
+        T &c = C[j * ldc + i];
+        if constexpr (std::is_same<T, __half>::value) c = beta == 0.f ? __float2half_rn(0.f) : __float2half_rn(beta * __half2float(c));
+        else if constexpr (std::is_same<T, int32_t>::value) c = beta == 0.f ? 0 : __float2int_rn(beta * (float)c);
+        else c = beta == 0.f ? 0.f : beta * c;
+    }
+}
+
 }  // namespace
+
+// hipBLAS GEMM with k == 0: C = beta * C (column-major m x n, ldc).
+int scale_c(void *C, int ctype, int64_t ldc, int m, int n, float beta, cudaStream_t stream) {
+    if (beta == 1.0f || m <= 0 || n <= 0) return VKF_OK;
+    const int64_t total = (int64_t)m * n;
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+    switch (ctype) {
+    case 0: scale_kernel<__half><<<grid, 256, 0, stream>>>((__half *)C, ldc, m, n, beta); break;
+    case 1: scale_kernel<float><<<grid, 256, 0, stream>>>((float *)C, ldc, m, n, beta); break;
+    case 3: scale_kernel<int32_t><<<grid, 256, 0, stream>>>((int32_t *)C, ldc, m, n, beta); break;
+    default: return VKF_ERR_UNSUPPORTED;
+    }
+    return check_launch();
+}
 
 int transpose(const void *src, int64_t lds, void *dst, int64_t ldd, int rows, int cols, int esize,
               cudaStream_t stream) {

@@ -18,7 +18,7 @@ namespace vkf {
 
 int gemv_launch_raw(int wtype, const void *W, const void *X, int64_t ldx_bytes, void *Y, int y_f16, int64_t ldy,
                     int M, int N, int K, cudaStream_t stream, float *ws, size_t ws_cap, int *cnt, size_t cnt_cap,
-                    int sms, unsigned *err);
+                    int sms, unsigned *err, int plan_only);
 
 namespace noalloc {
 
@@ -66,6 +66,24 @@ static int setup(int dev, Addrs **out) {
 }
 
 }  // namespace noalloc
+
+// Error bits the allocation-free kernels set on the current device (a bounded
+// wait gave up), read and cleared; 0 when the entry point was never used
+// there.  Called by vkflame_check_kernel_errors after it synchronised.
+int noalloc_take_errors(unsigned *bits) {
+    *bits = 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev >= noalloc::MAX_DEVICES) return VKF_ERR_NO_DEVICE;
+    noalloc::Addrs *ad = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(noalloc::g_mu);
+        if (!noalloc::g_addrs[dev].ready) return VKF_OK;
+        ad = &noalloc::g_addrs[dev];
+    }
+    if (cudaMemcpy(bits, ad->err, sizeof(unsigned), cudaMemcpyDeviceToHost) != cudaSuccess) return VKF_ERR_CUDA;
+    if (*bits && cudaMemset(ad->err, 0, sizeof(unsigned)) != cudaSuccess) return VKF_ERR_CUDA;
+    return VKF_OK;
+}
 }  // namespace vkf
 
 using namespace vkf;
@@ -94,11 +112,16 @@ extern "C" int vkflame_quant_linear_noalloc(const void *W, int wtype, const void
     if (rc) return set_status(rc);
     if (2 * ad->sms > noalloc::NOALLOC_MAX_CTAS) return set_status(VKF_ERR_UNSUPPORTED);
     cudaStream_t st = (cudaStream_t)stream;
+    // Plan first, so that a request the kernel cannot serve is refused before
+    // anything is queued on the stream.
+    rc = gemv_launch_raw(wtype, W, X, ldx * 2, Y, ytype == VKF_Y_F16, ldy, M, N, K, st, ad->ws, noalloc::WS_FLOATS,
+                         ad->cnt, noalloc::CNT_INTS, ad->sms, ad->err, 1);
+    if (rc) return set_status(rc);
     // The arrival counters must start at zero; a completed call leaves them
     // zero, but an interrupted one may not, so clear the ones this call uses.
     const size_t ncnt = (size_t)(N + 15) / 16;
     if (cudaMemsetAsync(ad->cnt, 0, ncnt * sizeof(int), st) != cudaSuccess) return set_status(VKF_ERR_CUDA);
-    rc = gemv_launch_raw(wtype, W, X, ldx * 2, Y, ytype == VKF_Y_F16, ldy, M, N, K, st, ad->ws,
-                         noalloc::WS_FLOATS, ad->cnt, noalloc::CNT_INTS, ad->sms, ad->err);
+    rc = gemv_launch_raw(wtype, W, X, ldx * 2, Y, ytype == VKF_Y_F16, ldy, M, N, K, st, ad->ws, noalloc::WS_FLOATS,
+                         ad->cnt, noalloc::CNT_INTS, ad->sms, ad->err, 0);
     return set_status(rc);
 }

@@ -22,6 +22,10 @@ struct DeviceState {
     unsigned *d_error = nullptr;  // kernels OR a VKF_KERR_* bit here when a bounded wait gives up
 };
 DeviceState *device_state();  // current device; nullptr if CUDA has no device
+DeviceState *existing_device_state();  // same, but never creates it (nullptr if not yet created)
+// Reads and clears the allocation-free entry point's kernel error bits on the
+// current device (noalloc.cu); *bits = 0 if it never ran there.
+int noalloc_take_errors(unsigned *bits);
 
 // Scratch memory for one stream on the current device (grows on demand,
 // zero-filled when (re)allocated).  Calls on one stream are ordered, so a

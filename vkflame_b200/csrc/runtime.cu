@@ -63,6 +63,13 @@ int check_launch() {
 static std::mutex g_dev_mu;
 static std::vector<DeviceState *> g_devs;
 
+DeviceState *existing_device_state() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    return dev < (int)g_devs.size() ? g_devs[dev] : nullptr;
+}
+
 DeviceState *device_state() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
@@ -305,17 +312,21 @@ const char *vkflame_status_string(int status) {
 }
 
 int vkflame_check_kernel_errors(void) {
-    DeviceState *st = device_state();
-    if (!st) return set_status(VKF_ERR_NO_DEVICE);
+    // Looks only at state that exists already, so a process that uses just the
+    // allocation-free entry point allocates nothing here either.
     if (cudaDeviceSynchronize() != cudaSuccess) return set_status(VKF_ERR_CUDA);
     unsigned bits = 0;
-    if (cudaMemcpy(&bits, st->d_error, sizeof(bits), cudaMemcpyDeviceToHost) != cudaSuccess)
-        return set_status(VKF_ERR_CUDA);
-    if (bits) {
-        cudaMemset(st->d_error, 0, sizeof(unsigned));
-        return set_status(VKF_ERR_TIMEOUT);
+    int rc = noalloc_take_errors(&bits);
+    if (rc) return set_status(rc);
+    DeviceState *st = existing_device_state();
+    if (st) {
+        unsigned b = 0;
+        if (cudaMemcpy(&b, st->d_error, sizeof(b), cudaMemcpyDeviceToHost) != cudaSuccess)
+            return set_status(VKF_ERR_CUDA);
+        if (b && cudaMemset(st->d_error, 0, sizeof(unsigned)) != cudaSuccess) return set_status(VKF_ERR_CUDA);
+        bits |= b;
     }
-    return set_status(VKF_OK);
+    return set_status(bits ? VKF_ERR_TIMEOUT : VKF_OK);
 }
 
 uint64_t vkflame_kernel_launch_count(void) { return g_launches.load(); }
