@@ -195,6 +195,9 @@ METRIC = "aggregate weight-streaming GB/s, 48-layer Qwen2-14B Q4_K_M linear stac
 # ncu captures of the Q4_K (K=5120, N=13824: 39.890 / 39.855 MB) and Q6_K
 # (K=13824, N=5120: 58.172 / 58.099 MB) shapes of the stack.
 GEMV_TRAFFIC_RATIO = 1.001
+# Same ratio for the per-token chain kernel (placeholder until its own
+# capture replaces it).
+CHAIN_TRAFFIC_RATIO = 1.001
 
 
 def stack_groups():
@@ -206,62 +209,153 @@ def stack_groups():
             ("down", S.Q6_K, FFN, HIDDEN, "f")]
 
 
-class Stack:
-    """One rank's column shard of the stack, run as a CUDA graph of GEMV
-    launches.  N = 1: vkflame_quant_linear_ex.  N > 1: each linear is
-    vkflame_quant_linear_gather, the decode GEMV fused with the all-gather
-    (every rank stores its output slice into all ranks' gathered buffers over
-    NVLink as {fp16 pair, epoch} words), and each linear's X is an earlier
-    linear's gathered output (the layer's data flow: qk and the previous down output
-    feed the next layer, o reads qk's, gate/up o's, down gate/up's, the head
-    the last down's), so every gather is waited for, word by word, inside the
-    kernel that reads it.  No NCCL call in the timed region."""
+def stack_links():
+    """The stack's linears in order: (name, qtype, K, N, input), the output
+    head last."""
+    return [g for _ in range(LAYERS) for g in stack_groups()] + [("head", S.Q6_K, HIDDEN, VOCAB, "h")]
 
-    def __init__(self, world, rank, dist, stream):
+
+def link_seed(rank: int, i: int) -> int:
+    """Seed of rank `rank`'s shard of stack link i (make_quant_weight_gpu)."""
+    return 1000 * rank + i + 1
+
+
+class Stack:
+    """One rank's column shard of the stack as ONE persistent kernel per token
+    (vkflame_chain_*).  Default dataflow "chained", the same at every N: each
+    linear reads an earlier linear's gathered output (qk and v the previous
+    layer's down, o qk's, gate/up o's, down gate/up's, the head the last
+    down's; the first layer's qk and v read the token's input row), and every rank
+    stores its output slice into all ranks' gathered buffers as {fp16 pair,
+    epoch} words (NVLink peer stores; world size 1: its own buffer), which the
+    consumers wait for word by word.  "independent" (world size 1 only): every
+    linear reads its layer input and writes a plain fp16 row, the pure
+    weight-streaming form.  "launches": the same chained dataflow as one
+    vkflame_quant_linear_gather launch per linear (N = 1: independent
+    vkflame_quant_linear_ex launches), for comparison."""
+
+    def __init__(self, world, rank, dist, stream, mode="chained", trace=False):
         import torch
         from vkflame_b200 import rt, shard
-        self.rt, self.world, self.rank, self.dist, self.stream = rt, world, rank, dist, stream
-        self.linears = []  # (qtype, K, Nshard, weight, input tensor, output, gather struct or None)
+        from vkflame_b200.gather import GatherGroup
+        self.rt, self.world, self.rank, self.dist, self.stream, self.mode = rt, world, rank, dist, stream, mode
         self.x_h = torch.randn((1, HIDDEN), device="cuda").half()
         self.x_f = torch.randn((1, FFN), device="cuda").half()
         self.weight_bytes = 0
-        self.gg = None
-        if world > 1:
-            from vkflame_b200.gather import GatherGroup
-            self.gg = GatherGroup(dist, world, rank)
-        seed = 1000 * rank
-        groups = [g for _ in range(LAYERS) for g in stack_groups()] + [("head", S.Q6_K, HIDDEN, VOCAB, "h")]
-        prev = []  # gathered outputs so far, newest last
-        for i, (name, q, K, N, inp) in enumerate(groups):
+        self.gg = GatherGroup(dist, world, rank)
+        self.links = []   # (name, q, K, n, weight, out buffer or plain tensor, x source index or -1)
+        self.ops = []     # "launches" mode: (q, K, n, w, x tensor, out, vkf_gather_t)
+        chain = []
+        for i, (name, q, K, N, inp) in enumerate(stack_links()):
             r0, r1 = shard.row_range(N, world, rank)  # this rank's output rows (vkflame_b200/shard.py)
             n = r1 - r0
-            seed += 1
-            w = make_quant_weight_gpu(q, n, K, seed)
-            if world > 1:
-                y = self.gg.buffer(N)
-                src = next((t for t in reversed(prev) if t.N >= K), None)
-                g = self.gg.op(y, x=src)
-                x = src.tensor if src is not None else (self.x_h if inp == "h" else self.x_f)
-                prev.append(y)
-            else:
-                y = torch.empty((1, n), device="cuda", dtype=torch.float16)
-                x, g = (self.x_h if inp == "h" else self.x_f), None
-            self.linears.append((q, K, n, w, x, y, g))
+            w = make_quant_weight_gpu(q, n, K, link_seed(rank, i))
             self.weight_bytes += w.numel()
-        self.out = self.linears[-1][5] if world == 1 else self.linears[-1][5].tensor
+            xin = self.x_h if inp == "h" else self.x_f
+            if mode == "independent":
+                y = torch.empty((1, n), device="cuda", dtype=torch.float16)
+                chain.append(self.gg.chain_linear(w.data_ptr(), q, K, n, None, x_plain=xin.data_ptr(),
+                                                  y_plain=y.data_ptr()))
+                self.links.append((name, q, K, n, w, y, -1))
+                continue
+            y = self.gg.buffer(N)
+            src = self._source(name)
+            if mode == "launches":
+                g = self.gg.op(y, x=self.links[src][5] if src >= 0 else None)
+                self.ops.append((q, K, n, w, self.links[src][5].tensor if src >= 0 else self.x_h, y, g))
+            chain.append(self.gg.chain_linear(w.data_ptr(), q, K, n, y, x_src=src,
+                                              x_plain=self.x_h.data_ptr() if src < 0 else 0))
+            self.links.append((name, q, K, n, w, y, src))
+        self.chain = None if mode == "launches" else rt.Chain(chain, world, rank, rt.CHAIN_TRACE if trace else 0)
+        last = self.links[-1][5]
+        self.out = last if mode == "independent" else last.tensor
         torch.cuda.synchronize()
-        barrier(dist)  # every rank's counters initialised before any kernel signals
+        barrier(dist)  # every rank's buffers zeroed before any kernel stores into them
+
+    def _source(self, name: str) -> int:
+        """Link whose gathered output is this link's X (-1: the token's input
+        row): qk and v read the layer input (the previous layer's down), o
+        reads qk (standing in for the attention output), gate/up o, down
+        gate/up, the head the last down."""
+        want = {"qk": "down", "v": "down", "o": "qk", "gate_up": "o", "down": "gate_up", "head": "down"}[name]
+        return next((j for j in range(len(self.links) - 1, -1, -1) if self.links[j][0] == want), -1)
 
     def step(self):
+        if self.chain is not None:
+            self.chain.run(self.stream)
+            return
         rt = self.rt
-        for q, K, n, w, x, y, g in self.linears:
-            if g is None:
-                rt.quant_linear_ex(w.data_ptr(), q, x.data_ptr(), rt.X_F16, y.data_ptr(), rt.Y_F16, 1, n, K, K, n,
-                                   rt.FLAG_STATIC_WEIGHTS, self.stream)
-            else:
-                ldx = x.shape[2] * 2 if g.x_gathered else x.shape[1]  # gathered X: words of 2 values
-                rt.quant_linear_gather(w.data_ptr(), q, x.data_ptr(), rt.Y_F16, 1, n, K, ldx, y.N,
-                                       rt.FLAG_STATIC_WEIGHTS, g, self.stream)
+        for q, K, n, w, x, y, g in self.ops:
+            ldx = x.shape[2] * 2 if g.x_gathered else x.shape[1]  # gathered X: words of 2 values
+            rt.quant_linear_gather(w.data_ptr(), q, x.data_ptr(), rt.Y_F16, 1, n, K, ldx, y.N,
+                                   rt.FLAG_STATIC_WEIGHTS, g, self.stream)
+
+    def runs(self) -> int:
+        """Completed runs (the chain's epoch; "launches": the first call site's)."""
+        if self.chain is not None:
+            return self.chain.epoch()
+        return int(self.gg.epochs[0].item())
+
+    def close(self):
+        if self.chain is not None:
+            self.chain.close()
+        self.gg.close()
+
+    # ---------------------------------------------------------- parity ----
+    def parity(self, sample=("o", "down", "head")):
+        """Checks of the last run's outputs, outside the timed region.
+        ranks_identical: every rank holds the same gathered words (a
+        position-weighted checksum per buffer, all-gathered).  vs_unsharded:
+        on rank 0, the full (unsharded) weights of sampled links regenerated
+        from every rank's seeds, run through the single-GPU decode GEMV
+        (vkflame_quant_linear_ex) on the same gathered input, against the
+        gathered output; normwise max |y - r| / max |r|."""
+        import torch
+        from vkflame_b200 import shard
+        if self.mode == "independent":
+            return None
+        ep = self.runs()
+        words = [lk[5].tensor[ep & 1] for lk in self.links]  # [1][N/2][2] int32
+        sums = []
+        for wds in words:
+            v = wds.reshape(-1).to(torch.int64)
+            pos = torch.arange(1, v.numel() + 1, device=v.device, dtype=torch.int64)
+            sums.append(((v & 0xFFFFFFFF) * pos).remainder_(2 ** 61 - 1).sum())
+        local = torch.stack(sums)
+        epochs_ok = all(bool((wds[..., 1] == ep).all()) for wds in words)
+        if self.world > 1:
+            allv = [torch.empty_like(local) for _ in range(self.world)]
+            self.dist.all_gather(allv, local)
+            same = all(bool(torch.equal(allv[0], a)) for a in allv)
+        else:
+            same = True
+        out = {"ranks_identical": same, "epochs_current": epochs_ok, "runs": ep}
+        if self.rank != 0:
+            return out
+        errs = {}
+        names = [lk[0] for lk in self.links]
+        picks = [names.index(sample[0]), len(names) - 1 - names[::-1].index(sample[1]), names.index(sample[2])]
+        for i in picks:
+            name, q, K, n, w, y, src = self.links[i]
+            N = n * self.world
+            wfull = torch.cat([make_quant_weight_gpu(q, shard.row_range(N, self.world, r)[1] -
+                                                     shard.row_range(N, self.world, r)[0], K, link_seed(r, i))
+                               for r in range(self.world)]) if self.world > 1 else w
+            xin = (self.x_h if src < 0 else self.links[src][5].tensor[ep & 1][..., 0].contiguous().view(
+                torch.float16).reshape(1, -1)[:, :K]).contiguous()
+            ref = torch.empty((1, N), device="cuda", dtype=torch.float16)
+            self.rt.quant_linear_ex(wfull.data_ptr(), q, xin.data_ptr(), self.rt.X_F16, ref.data_ptr(),
+                                    self.rt.Y_F16, 1, N, K, K, N, 0, self.stream)
+            torch.cuda.synchronize()
+            got = words[i][..., 0].contiguous().view(torch.float16).reshape(1, -1).double()
+            r = ref.double()
+            errs[f"{name}#{i}"] = float((got - r).abs().max() / r.abs().max().clamp_min(1e-30))
+            del wfull
+        tol = 1e-3
+        out["vs_unsharded"] = {"links": errs, "max_normwise_err": max(errs.values()), "tol": tol,
+                               "reference": "vkflame_quant_linear_ex on the full weights (one GPU)",
+                               "pass": max(errs.values()) < tol}
+        return out
 
 
 def timed_graph(graph, stream, steps):
@@ -274,57 +368,79 @@ def timed_graph(graph, stream, steps):
     return e0, e1
 
 
-def bench_stack(args, world, rank, local, dist):
+def run_stack(args, world, rank, local, dist, mode, steps, e2e=True, trace=False):
+    """Builds the stack, captures one token as a CUDA graph, times `steps`
+    replays (max over ranks) and, optionally, the end-to-end step."""
     import torch
     from vkflame_b200 import rt
-    rt.lib()
     s = torch.cuda.Stream()
+    res = {}
     with torch.cuda.stream(s):
-        st = Stack(world, rank, dist, s.cuda_stream)
-        torch.cuda.synchronize()
-        st.step()  # warms NCCL and the kernels' one-time setup before capture
+        st = Stack(world, rank, dist, s.cuda_stream, mode=mode, trace=trace)
+        st.step()  # one-time setup outside the capture
         torch.cuda.synchronize()
         l0 = rt.launch_count()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
             st.step()
-        launches_per_step = rt.launch_count() - l0
+        res["launches_per_step"] = rt.launch_count() - l0
         for _ in range(args.warmup):
             g.replay()
         barrier(dist)
         sampler = ClockSampler(local)
         sampler.start()
-        e0, e1 = timed_graph(g, s, args.steps)
+        e0, e1 = timed_graph(g, s, steps)
         barrier(dist)
-        clocks = sampler.stop()
-        ms = max_over_ranks(dist, e0.elapsed_time(e1) / args.steps)
+        res["clocks"] = sampler.stop()
+        res["ms"] = max_over_ranks(dist, e0.elapsed_time(e1) / steps)
         rt.check_kernel_errors()
+        res["parity"] = st.parity()
+        if trace and st.chain is not None:
+            res["trace"] = st.chain.trace()
+        if e2e:
+            # End to end through the public API with host buffers: pinned token
+            # activations -> device, the stack, output-head logits -> pinned host
+            # (chained: the head's gathered buffers, {fp16 pair, epoch} words).
+            xh = torch.randn((1, HIDDEN)).half().pin_memory()
+            outh = torch.empty(st.out.shape, dtype=st.out.dtype).pin_memory()
+            def e2e_step():
+                st.x_h.copy_(xh, non_blocking=True)
+                g.replay()
+                outh.copy_(st.out, non_blocking=True)
+            for _ in range(args.warmup):
+                e2e_step()
+            barrier(dist)
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            f0.record(s)
+            for _ in range(steps):
+                e2e_step()
+            f1.record(s)
+            barrier(dist)
+            res["e2e_ms"] = max_over_ranks(dist, f0.elapsed_time(f1) / steps)
+            res["d2h"] = int(st.out.numel()) * st.out.element_size()
+        res["weight_bytes"] = st.weight_bytes
+        torch.cuda.synchronize()
+        st.close()
+        del st, g
+        torch.cuda.empty_cache()
+    return res
 
-        # End to end through the public API with host buffers: pinned token
-        # activations -> device, the stack, output-head logits -> pinned host.
-        xh = torch.randn((1, HIDDEN)).half().pin_memory()
-        # N > 1: the head's gathered buffers ({fp16 pair, epoch} words, both parities)
-        outh = torch.empty(st.out.shape, dtype=st.out.dtype).pin_memory()
-        def e2e_step():
-            st.x_h.copy_(xh, non_blocking=True)
-            g.replay()
-            outh.copy_(st.out, non_blocking=True)
-        for _ in range(args.warmup):
-            e2e_step()
-        barrier(dist)
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        f0.record(s)
-        for _ in range(args.steps):
-            e2e_step()
-        f1.record(s)
-        barrier(dist)
-        ems = max_over_ranks(dist, f0.elapsed_time(f1) / args.steps)
 
-    total_bytes = st.weight_bytes * world  # every rank streams its shard once per token
+def bench_stack(args, world, rank, local, dist):
+    res = run_stack(args, world, rank, local, dist, args.stack_mode, args.steps, trace=args.trace)
+    extra = {}
+    if world == 1 and not args.no_extras and args.stack_mode == "chained":
+        ind = run_stack(args, world, rank, local, dist, "independent", args.steps, e2e=False)
+        extra["independent_ms_per_token"] = ind["ms"]
+        extra["independent_gb_s"] = ind["weight_bytes"] / (ind["ms"] * 1e-3) / 1e9
+    ms, ems = res["ms"], res["e2e_ms"]
+    weight_bytes = res["weight_bytes"]
+    total_bytes = weight_bytes * world  # every rank streams its shard once per token
     value = total_bytes / (ms * 1e-3) / 1e9
     peaks = measured_peaks()
     peak = peaks.get("hbm_gbs") or HBM_FALLBACK_GBS
-    per_gpu = st.weight_bytes / (ms * 1e-3) / 1e9
+    per_gpu = weight_bytes / (ms * 1e-3) / 1e9
+    chained = args.stack_mode != "independent"
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
@@ -333,24 +449,30 @@ def bench_stack(args, world, rank, local, dist):
         "config": {"workload": "config 5: Qwen2-14B linear stack, 48 layers + output head, M=1 decode",
                    "layers": LAYERS, "hidden": HIDDEN, "ffn": FFN, "vocab": VOCAB,
                    "weight_gb_per_token": total_bytes / 1e9, "column_shards": world,
-                   "launches_per_token": launches_per_step,
-                   "dataflow": ("chained: each linear reads an earlier linear's gathered output" if world > 1
-                             else "independent: each linear reads its layer input"),
-                "collective": ("all-gather fused into each GEMV: output slices stored into every rank's buffer over "
-                                  "NVLink (CUDA IPC peer memory) as {fp16 pair, epoch} words, waited for word by word "
-                                  "in the kernel that reads them") if world > 1 else "none",
-                   "l2": "weights (9.0 GB) exceed L2; no flush needed"},
+                   "kernel": ("one persistent kernel per token (vkflame_chain_run)" if args.stack_mode != "launches"
+                              else "one decode GEMV launch per linear"),
+                   "launches_per_token": res["launches_per_step"],
+                   "dataflow": ("chained at every N: each linear reads an earlier linear's gathered output"
+                                if chained else "independent: each linear reads its layer input"),
+                   "collective": ("all-gather fused into the decode: output slices stored into every rank's "
+                                  "buffer over NVLink (CUDA IPC peer memory) as {fp16 pair, epoch} words, "
+                                  "waited for word by word by the linear that reads them") if world > 1 else "none",
+                   "l2": "weights (9.0 GB) exceed L2; no flush needed", **extra},
         "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks.get("hbm_gbs") else "fallback",
-                     "traffic": st.weight_bytes / launches_per_step * GEMV_TRAFFIC_RATIO,
-                     "note": "dominant kernel = gemv_kernel, every launch of the timed graph: algorithmic weight "
-                             "bytes per launch / average launch time (graph time / launches); traffic = DRAM "
-                             "bytes per launch, from the ncu captures of the same kernel on the stack's shapes "
-                             "(ratio to algorithmic bytes, profiles/gemv_*.md)"},
+                     "traffic": weight_bytes * CHAIN_TRAFFIC_RATIO,
+                     "note": "dominant kernel = the per-token chain kernel (the only launch of the timed graph): "
+                             "algorithmic weight bytes per launch (this rank's shard of the token) / launch time; "
+                             "traffic = DRAM bytes per launch scaled from an ncu capture of the same kernel"},
         "e2e": {"value": total_bytes / (ems * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": HIDDEN * 2,
-                "d2h_bytes_per_step": int(st.out.numel()) * st.out.element_size(), "ms_per_step": ems},
-        "gpu_launches": launches_per_step * args.steps, "clocks": clocks,
+                "d2h_bytes_per_step": res["d2h"], "ms_per_step": ems},
+        "parity": res["parity"],
+        "gpu_launches": res["launches_per_step"] * args.steps, "clocks": res["clocks"],
     }
+    if "trace" in res:
+        out = ROOT / "gpurun_out"
+        out.mkdir(exist_ok=True)
+        np.save(out / f"chain_trace_w{world}_r{rank}.npy", res["trace"])
     return line
 
 
@@ -482,13 +604,15 @@ def cpu_baseline_stack(budget_s=12.0):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="stack", choices=["stack"] + list(SUB_CASES),
                     help="stack (config 5, the headline) or one config 1-4 case alone (device time only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 1-4 sub-benchmarks")
+    ap.add_argument("--stack-mode", default="chained", choices=["chained", "independent", "launches"])
+    ap.add_argument("--trace", action="store_true", help="record per-linear chain timestamps (gpurun_out/)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_env()

@@ -157,6 +157,42 @@ typedef struct vkf_gather {
 int vkflame_quant_linear_gather(const void *W, int wtype, const void *X, int ytype, int M, int N, int K,
                                 int64_t ldx, int64_t ldy, unsigned flags, const vkf_gather_t *g, void *stream);
 
+/* ---- a token's decode linears as one persistent kernel (M = 1) ----------
+ * No counterpart in the reference.  The linears of one decode step, in
+ * order, each computing this rank's shard (rows [0, N) of W) of
+ * Y = X dequant(W)^T and storing it into every rank's gathered buffers (the
+ * vkf_gather_t word layout above; world size 1: the local buffer) or, at
+ * world size 1, into a plain fp16 row.  X is a plain fp16 row (x_src = -1)
+ * or the gathered output of an earlier linear of the same chain (x_src = its
+ * index; its first K values).  vkflame_chain_run makes ONE cooperative
+ * launch (one CTA per SM) that walks every linear: weights stream ahead
+ * across linear boundaries while each linear waits (bounded, inside the
+ * kernel) for the words of its X.  Formats Q4_K, Q5_K, Q6_K; K a multiple of
+ * 256; N even.  One run per step; ranks run the same chain in the same
+ * order; the gathered buffers are zeroed on every rank before the first run
+ * (host barrier).  The chain owns its run count (epoch) and scratch. */
+typedef struct vkf_chain_linear {
+    const void *W;                   /* this rank's rows, ggml blocks                        */
+    int wtype;                       /* VKF_DEQUANT_Q4_K, Q5_K or Q6_K                        */
+    int K, N;                        /* input length; rows of this rank's shard               */
+    int x_src;                       /* -1: x_plain; else index of an earlier linear          */
+    const void *x_plain;             /* fp16 row of K values, 16-byte aligned                 */
+    void *y_rank[VKF_MAX_RANKS];     /* gathered output: each rank's buffer 0, at this rank's first word */
+    int64_t y_stride;                /* bytes from a rank's buffer 0 to its buffer 1          */
+    void *y_plain;                   /* world size 1 only: plain fp16 output row instead      */
+} vkf_chain_linear_t;
+typedef struct vkf_chain vkf_chain_t;
+#define VKF_CHAIN_TRACE 1u           /* record per-linear timestamps (vkflame_chain_trace)   */
+int vkflame_chain_create(const vkf_chain_linear_t *linears, int n, int world, int rank, unsigned flags,
+                         vkf_chain_t **chain);
+int vkflame_chain_run(vkf_chain_t *chain, void *stream);
+/* Run count of the chain's completed runs (synchronous read). */
+int vkflame_chain_epoch(const vkf_chain_t *chain, int *epoch);
+/* VKF_CHAIN_TRACE: per linear {latest time a CTA had its X ready, latest
+ * output store} of the last run, globaltimer ns (host array of 2n). */
+int vkflame_chain_trace(const vkf_chain_t *chain, unsigned long long *times);
+int vkflame_chain_destroy(vkf_chain_t *chain);
+
 /* CUDA IPC for the gathered buffers and counters: a 64-byte handle of the
  * allocation holding dev_ptr plus dev_ptr's byte offset in it; open returns
  * the allocation's base mapped in this process (add the offset). */
@@ -204,6 +240,64 @@ int vkflame_quantize_q8_1(const float *x, void *y, int M, int K, int64_t ldx, vo
 int vkflame_linear_int8(const int8_t *X, const int8_t *W, const float *sx, const float *sw,
                         const void *bias, void *Y, int32_t *acc_out, int M, int N, int K,
                         int activation, void *stream);
+
+/* ---- the rest of ggml's kernel-name table (runtime/dispatch.h:60-125) ----
+ * fp32 unless stated; pointers are device pointers.  Each restates the
+ * reference shader of the same name.  These entry points carry no stream
+ * argument (as in the reference): they launch on the calling thread's
+ * stream, set with vkflame_set_stream (NULL, the default: the legacy
+ * default stream).  vkflame_set_stream has no reference counterpart. */
+int vkflame_set_stream(void *stream);
+/* VKF_EW_* op ids of runtime/dispatch.h:24-38 (kernels/elementwise_f32.glsl). */
+#define VKF_EW_SILU 0
+#define VKF_EW_GELU_ERF 1
+#define VKF_EW_RELU 2
+#define VKF_EW_TANH 3
+#define VKF_EW_GELU_QUICK 4
+#define VKF_EW_NEG 5
+#define VKF_EW_SIGMOID 6
+#define VKF_EW_SQR 7
+#define VKF_EW_SQRT 8
+#define VKF_EW_EXP 9
+#define VKF_EW_LOG 10
+#define VKF_EW_ABS 11
+#define VKF_EW_SGN 12
+#define VKF_EW_HARDSIGMOID 13
+#define VKF_EW_HARDSWISH 14
+/* VKF_BINOP_* (runtime/dispatch.h:41-44; kernels/binop_f32.glsl). */
+#define VKF_BINOP_ADD 0
+#define VKF_BINOP_MUL 1
+#define VKF_BINOP_SUB 2
+#define VKF_BINOP_DIV 3
+/* runtime/dispatch.h:94-98: dst[i] = op(src[i]), i < n (in place allowed). */
+int vkflame_dispatch_elementwise_f32(void *ctx, const void *src, void *dst, uint32_t n, uint32_t op);
+/* runtime/dispatch.h:107-111: dst[i] = scale * src[i] + bias. */
+int vkflame_dispatch_scale_f32(void *ctx, const void *src, void *dst, uint32_t n, float scale, float bias);
+/* runtime/dispatch.h:113-117: dst[i] = op(src0[i], src1[i % src1_n]); x / 0 = 0. */
+int vkflame_dispatch_binop_f32(void *ctx, const void *src0, const void *src1, void *dst, uint32_t n,
+                               uint32_t src1_n, uint32_t op);
+/* runtime/dispatch.h:119-123: per row of N, y = x / sqrt(mean(x^2) + eps). */
+int vkflame_dispatch_rms_norm_f32(void *ctx, const void *src, void *dst, uint32_t M, uint32_t N, float eps);
+/* runtime/dispatch.h:66-69: fp16 X, gamma, Y: y = fp16(x * rrms * gamma). */
+int vkflame_dispatch_rms_norm(void *ctx, const void *X, const void *gamma, void *Y, int M, int N, float eps);
+/* runtime/dispatch.h:71-74: row softmax, M rows of N. */
+int vkflame_dispatch_softmax(void *ctx, const void *X, void *Y, int M, int N);
+/* runtime/dispatch.h:100-105: neox RoPE of n_seqs x ne1 rows of ne0 values:
+ * value j pairs with j + ne0/2, theta = pos[seq] * theta_scale^j *
+ * freq_scale for 2j < n_dims (pass-through beyond).  Every row and pair is
+ * computed (the reference's grid, ne1 x n_seqs workgroups for a shader
+ * indexed by rows in x and pair groups in y, reached only part of them,
+ * runtime/dispatch.cpp:545-548); p0, p1 unused. */
+int vkflame_dispatch_rope_neox(void *ctx, const void *src, const void *pos, void *dst, uint32_t ne0, uint32_t ne1,
+                               uint32_t n_dims, uint32_t n_seqs, float theta_scale, float freq_scale, uint32_t p0,
+                               uint32_t p1);
+/* runtime/dispatch.h:81-84: fp16 weight [V x D], int32 indices [B], fp16
+ * out [B x D]; an index outside [0, V) gives a zero row. */
+int vkflame_dispatch_embedding(void *ctx, const void *weight, const void *indices, void *out, int V, int D, int B);
+/* ggml get_rows into fp32 (no reference entry point; the hipLaunchKernel
+ * get_rows branch): weight fp32 (weight_f32 = 1) or fp16 [V x D]. */
+int vkflame_get_rows(const void *weight, int weight_f32, const void *indices, float *out, int V, int D, int B,
+                     void *stream);
 
 /* ---- diagnostics -------------------------------------------------------- */
 int vkflame_get_last_error(void);

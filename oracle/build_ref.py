@@ -35,6 +35,10 @@ SHADERS = [
     "dequant_q4_0", "dequant_q4_1", "dequant_q5_0", "dequant_q8_0", "dequant_q8_1",
     "dequant_q4_k", "dequant_q5_k", "dequant_q6_k",
     "linear_int8", "linear_fp16", "linear_fp16_fp32out",
+    # the non-matmul kernels of the hipLaunchKernel table that need no
+    # subgroup operations (rms_norm*.glsl and softmax_online.glsl reduce with
+    # subgroup intrinsics, which this invocation-at-a-time harness cannot run)
+    "elementwise_f32", "scale_f32", "binop_f32", "rope_neox", "embedding",
 ]
 
 PRELUDE = r"""
@@ -55,6 +59,7 @@ static inline vec2 unpackHalf2x16(uint v) {
 template <class T> static inline T clamp(T v, T lo, T hi) { return v < lo ? lo : (v > hi ? hi : v); }
 static inline float sign(float x) { return x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : 0.0f); }
 using std::abs; using std::exp; using std::max; using std::min; using std::round;
+using std::tanh; using std::sqrt; using std::log; using std::pow; using std::cos; using std::sin;
 """
 
 FLOAT_LIT = re.compile(r"(?<![\w.])((?:\d+\.\d*|\.\d+)(?:[eE][+-]?\d+)?)(?![\w.])")

@@ -345,3 +345,127 @@ int oracle_quant_linear(int wtype, const void *w, int xtype, const void *x,
     free(xf);
     return 0;
 }
+
+/* ---- the non-matmul kernels of the hipLaunchKernel table ---------------- */
+
+/* kernels/elementwise_f32.glsl:20-26: erf by A&S 7.1.26 with sign(x). */
+static float erf_ew(float x) {
+    float t = 1.0f / (1.0f + 0.3275911f * fabsf(x));
+    float p = t * (0.254829592f + t * (-0.284496736f + t * (1.421413741f + t * (-1.453152027f + t * 1.061405429f))));
+    float s = x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : 0.0f);
+    return s * (1.0f - p * expf(-x * x));
+}
+
+static float clampf01(float v) { return v < 0.0f ? 0.0f : (v > 1.0f ? 1.0f : v); }
+
+/* kernels/elementwise_f32.glsl:33-50 (op ids 0..14). */
+float oracle_unary(int op, float x) {
+    switch (op) {
+    case 0: return x / (1.0f + expf(-x));
+    case 1: return 0.5f * x * (1.0f + erf_ew(x * 0.7071067811865476f));
+    case 2: return x < 0.0f ? 0.0f : x;  /* max(x, 0.0): -0 stays -0 */
+    case 3: return tanhf(x);
+    case 4: return x * (1.0f / (1.0f + expf(-1.702f * x)));
+    case 5: return -x;
+    case 6: return 1.0f / (1.0f + expf(-x));
+    case 7: return x * x;
+    case 8: return sqrtf(x);
+    case 9: return expf(x);
+    case 10: return logf(x);
+    case 11: return fabsf(x);
+    case 12: return x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : 0.0f);
+    case 13: return clampf01((x + 3.0f) / 6.0f);
+    case 14: return x * clampf01((x + 3.0f) / 6.0f);
+    default: return x;
+    }
+}
+
+void oracle_elementwise(int op, const float *x, float *y, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) y[i] = oracle_unary(op, x[i]);
+}
+
+/* kernels/scale_f32.glsl:17-19 */
+void oracle_scale(const float *x, float *y, int64_t n, float scale, float bias) {
+    for (int64_t i = 0; i < n; ++i) y[i] = scale * x[i] + bias;
+}
+
+/* kernels/binop_f32.glsl:19-31 (src1 broadcast as i % src1_n; x / 0 = 0) */
+void oracle_binop(int op, const float *a, const float *b, float *y, int64_t n, int64_t bn) {
+    for (int64_t i = 0; i < n; ++i) {
+        float u = a[i], v = b[i % bn];
+        y[i] = op == 0 ? u + v : op == 1 ? u * v : op == 2 ? u - v : op == 3 ? (v != 0.0f ? u / v : 0.0f) : u;
+    }
+}
+
+/* kernels/rms_norm_f32.glsl:23-57: y = x * inversesqrt(sum(x^2)/N + eps).
+ * The shader sums per thread, then per subgroup, then across subgroups;
+ * this sums in double, so agreement is to fp32 rounding, not bit for bit. */
+void oracle_rms_norm_f32(const float *x, float *y, int M, int N, float eps) {
+    for (int m = 0; m < M; ++m) {
+        double s = 0.0;
+        for (int c = 0; c < N; ++c) s += (double)x[(int64_t)m * N + c] * x[(int64_t)m * N + c];
+        float r = (float)(1.0 / sqrt(s / N + (double)eps));
+        for (int c = 0; c < N; ++c) y[(int64_t)m * N + c] = x[(int64_t)m * N + c] * r;
+    }
+}
+
+/* kernels/rms_norm.glsl: fp16 x and gamma, y = fp16(x * rrms * gamma). */
+void oracle_rms_norm_f16(const uint16_t *x, const uint16_t *g, uint16_t *y, int M, int N, float eps) {
+    for (int m = 0; m < M; ++m) {
+        double s = 0.0;
+        for (int c = 0; c < N; ++c) {
+            double v = oracle_half_to_float(x[(int64_t)m * N + c]);
+            s += v * v;
+        }
+        float r = (float)(1.0 / sqrt(s / N + (double)eps));
+        for (int c = 0; c < N; ++c)
+            y[(int64_t)m * N + c] = oracle_float_to_half(oracle_half_to_float(x[(int64_t)m * N + c]) * r *
+                                                         oracle_half_to_float(g[c]));
+    }
+}
+
+/* kernels/softmax_online.glsl: y = exp(x - max) / sum(exp(x - max)) per row
+ * (the shader's online (max, d) merge equals this up to rounding). */
+void oracle_softmax(const float *x, float *y, int M, int N) {
+    for (int m = 0; m < M; ++m) {
+        const float *r = x + (int64_t)m * N;
+        float mx = -1e38f;
+        for (int c = 0; c < N; ++c) mx = r[c] > mx ? r[c] : mx;
+        double d = 0.0;
+        for (int c = 0; c < N; ++c) d += exp((double)r[c] - mx);
+        for (int c = 0; c < N; ++c) y[(int64_t)m * N + c] = (float)(exp((double)r[c] - mx) / d);
+    }
+}
+
+/* kernels/rope_neox.glsl:28-61 over every row and pair (rows [seq][head]). */
+void oracle_rope_neox(const float *x, const int32_t *pos, float *y, int ne0, int ne1, int n_dims, int n_seqs,
+                      float theta_scale, float freq_scale) {
+    int half = ne0 / 2;
+    for (int row = 0; row < ne1 * n_seqs; ++row)
+        for (int j = 0; j < half; ++j) {
+            int64_t b = (int64_t)row * ne0;
+            float x0 = x[b + j], x1 = x[b + j + half];
+            if (2 * j >= n_dims) {
+                y[b + j] = x0;
+                y[b + j + half] = x1;
+                continue;
+            }
+            float theta = (float)pos[row / ne1] * powf(theta_scale, (float)j) * freq_scale;
+            float c = cosf(theta), s = sinf(theta);
+            y[b + j] = x0 * c - x1 * s;
+            y[b + j + half] = x0 * s + x1 * c;
+        }
+}
+
+/* kernels/embedding.glsl:16-31: out[b] = weight[idx[b]], zeros out of range
+ * (esize 2: fp16 table and output; 4: fp32). */
+void oracle_embedding(const void *w, int esize, const int32_t *idx, void *out, int V, int D, int B) {
+    for (int b = 0; b < B; ++b) {
+        int r = idx[b];
+        for (int c = 0; c < D; ++c) {
+            uint8_t *o = (uint8_t *)out + ((int64_t)b * D + c) * esize;
+            if (r < 0 || r >= V) memset(o, 0, esize);
+            else memcpy(o, (const uint8_t *)w + ((int64_t)r * D + c) * esize, esize);
+        }
+    }
+}

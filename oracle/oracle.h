@@ -68,6 +68,19 @@ int oracle_quant_linear(int wtype, const void *w, int xtype, const void *x,
 /* Activation as the reference shaders define it (linear_fp16.glsl:23-36). */
 float oracle_activation(int act, float x);
 
+/* The non-matmul kernels of the hipLaunchKernel name table (fp32 unless
+ * stated); each restates the shader it names. */
+float oracle_unary(int op, float x);                                       /* elementwise_f32.glsl */
+void oracle_elementwise(int op, const float *x, float *y, int64_t n);
+void oracle_scale(const float *x, float *y, int64_t n, float scale, float bias);      /* scale_f32.glsl */
+void oracle_binop(int op, const float *a, const float *b, float *y, int64_t n, int64_t bn); /* binop_f32.glsl */
+void oracle_rms_norm_f32(const float *x, float *y, int M, int N, float eps);         /* rms_norm_f32.glsl */
+void oracle_rms_norm_f16(const uint16_t *x, const uint16_t *g, uint16_t *y, int M, int N, float eps); /* rms_norm.glsl */
+void oracle_softmax(const float *x, float *y, int M, int N);                         /* softmax_online.glsl */
+void oracle_rope_neox(const float *x, const int32_t *pos, float *y, int ne0, int ne1, int n_dims, int n_seqs,
+                      float theta_scale, float freq_scale);                          /* rope_neox.glsl */
+void oracle_embedding(const void *w, int esize, const int32_t *idx, void *out, int V, int D, int B); /* embedding.glsl */
+
 #ifdef __cplusplus
 }
 #endif

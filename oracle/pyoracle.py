@@ -180,3 +180,138 @@ def ref_linear_fp16(a, b, act=0, fp32out_shader=False):
     fn = ref().vkref_linear_fp16_fp32out if fp32out_shader else ref().vkref_linear_fp16
     fn(binds, C.c_void_p(_p(pc)), (N + 15) // 16, (M + 15) // 16, 1)
     return out
+
+
+# ---- the non-matmul kernels of the hipLaunchKernel table -------------------
+
+def _f32(a):
+    return np.ascontiguousarray(a, np.float32)
+
+
+def _sig(name, args, res=None):
+    fn = getattr(lib(), name)
+    fn.argtypes = args
+    fn.restype = res
+    return fn
+
+
+def elementwise(op: int, x: np.ndarray) -> np.ndarray:
+    x = _f32(x)
+    y = np.empty_like(x)
+    _sig("oracle_elementwise", [C.c_int, C.c_void_p, C.c_void_p, C.c_int64])(op, _p(x), _p(y), x.size)
+    return y
+
+
+def scale(x, s, b):
+    x = _f32(x)
+    y = np.empty_like(x)
+    _sig("oracle_scale", [C.c_void_p, C.c_void_p, C.c_int64, C.c_float, C.c_float])(_p(x), _p(y), x.size, s, b)
+    return y
+
+
+def binop(op, a, b):
+    a, b = _f32(a), _f32(b)
+    y = np.empty_like(a)
+    _sig("oracle_binop", [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64])(
+        op, _p(a), _p(b), _p(y), a.size, b.size)
+    return y
+
+
+def rms_norm_f32(x, eps):
+    x = _f32(x)
+    y = np.empty_like(x)
+    M, N = x.shape
+    _sig("oracle_rms_norm_f32", [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_float])(_p(x), _p(y), M, N, eps)
+    return y
+
+
+def rms_norm_f16(x, g, eps):
+    x = np.ascontiguousarray(x, np.float16)
+    g = np.ascontiguousarray(g, np.float16)
+    y = np.empty_like(x)
+    M, N = x.shape
+    _sig("oracle_rms_norm_f16", [C.c_void_p] * 3 + [C.c_int, C.c_int, C.c_float])(_p(x), _p(g), _p(y), M, N, eps)
+    return y
+
+
+def softmax(x):
+    x = _f32(x)
+    y = np.empty_like(x)
+    M, N = x.shape
+    _sig("oracle_softmax", [C.c_void_p, C.c_void_p, C.c_int, C.c_int])(_p(x), _p(y), M, N)
+    return y
+
+
+def rope_neox(x, pos, ne0, ne1, n_dims, n_seqs, theta_scale, freq_scale):
+    x = _f32(x)
+    pos = np.ascontiguousarray(pos, np.int32)
+    y = np.empty_like(x)
+    _sig("oracle_rope_neox", [C.c_void_p, C.c_void_p, C.c_void_p] + [C.c_int] * 4 + [C.c_float] * 2)(
+        _p(x), _p(pos), _p(y), ne0, ne1, n_dims, n_seqs, theta_scale, freq_scale)
+    return y
+
+
+def embedding(w, idx):
+    w = np.ascontiguousarray(w)
+    idx = np.ascontiguousarray(idx, np.int32)
+    V, D = w.shape
+    out = np.empty((idx.size, D), w.dtype)
+    _sig("oracle_embedding", [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p] + [C.c_int] * 3)(
+        _p(w), w.itemsize, _p(idx), _p(out), V, D, idx.size)
+    return out
+
+
+def _u32(*vals):
+    """Push-constant words: ints as uint32, floats as their fp32 bits."""
+    out = np.zeros(max(4, len(vals)), np.uint32)
+    for i, v in enumerate(vals):
+        out[i] = np.array([v], np.float32).view(np.uint32)[0] if isinstance(v, float) else v
+    return out
+
+
+def ref_elementwise(op, x):
+    """kernels/elementwise_f32.glsl (grid per runtime/dispatch.cpp:519-521)."""
+    x = _f32(x).ravel()
+    y = np.zeros_like(x)
+    pc = _u32(x.size, op)
+    ref().vkref_elementwise_f32((C.c_void_p * 2)(_p(x), _p(y)), C.c_void_p(_p(pc)), (x.size + 255) // 256, 1, 1)
+    return y
+
+
+def ref_scale(x, s, b):
+    x = _f32(x).ravel()
+    y = np.zeros_like(x)
+    pc = _u32(x.size, float(s), float(b))
+    ref().vkref_scale_f32((C.c_void_p * 2)(_p(x), _p(y)), C.c_void_p(_p(pc)), (x.size + 255) // 256, 1, 1)
+    return y
+
+
+def ref_binop(op, a, b):
+    a, b = _f32(a).ravel(), _f32(b).ravel()
+    y = np.zeros_like(a)
+    pc = _u32(a.size, op, b.size, 0)
+    ref().vkref_binop_f32((C.c_void_p * 3)(_p(a), _p(b), _p(y)), C.c_void_p(_p(pc)), (a.size + 255) // 256, 1, 1)
+    return y
+
+
+def ref_rope_neox(x, pos, ne0, ne1, n_dims, n_seqs, theta_scale, freq_scale):
+    """kernels/rope_neox.glsl over the grid its own header states (rows in x,
+    64-pair groups in y), which covers every row and pair."""
+    x = _f32(x).ravel()
+    pos = np.ascontiguousarray(pos, np.int32)
+    y = np.zeros_like(x)
+    pc = _u32(ne0, ne1, n_dims, n_seqs, float(theta_scale), float(freq_scale), 0, 0)
+    ref().vkref_rope_neox((C.c_void_p * 3)(_p(x), _p(pos), _p(y)), C.c_void_p(_p(pc)), ne1 * n_seqs,
+                          (ne0 // 2 + 63) // 64, 1)
+    return y
+
+
+def ref_embedding(w16, idx):
+    w = np.ascontiguousarray(w16, np.float16)
+    idx = np.ascontiguousarray(idx, np.int32)
+    V, D = w.shape
+    out = np.zeros((idx.size, D), np.float16)
+    pc = _u32(V, D, idx.size)
+    ref().vkref_embedding((C.c_void_p * 3)(_p(w), _p(idx), _p(out)), C.c_void_p(_p(pc)),
+                          (idx.size * D + 255) // 256, 1, 1)
+    return out

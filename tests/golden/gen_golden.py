@@ -89,6 +89,29 @@ def main() -> int:
     for act in range(4):
         data[f"f16_out_act{act}"] = po.ref_linear_fp16(a3, b3, act)
 
+    # The non-matmul kernels of the hipLaunchKernel table.  Inputs include
+    # zeros, negatives, large magnitudes and values where the ops saturate.
+    ew = np.concatenate([np.array([0.0, -0.0, 1.0, -1.0, 3.0, -3.0, 20.0, -20.0, 88.0, -88.0, 1e-30, 0.5],
+                                  np.float32), (rng.standard_normal(500) * 4).astype(np.float32)])
+    data["ew_in"] = ew
+    for op in range(15):
+        data[f"ew_out_op{op}"] = po.ref_elementwise(op, np.abs(ew) if op in (8, 10) else ew)
+    data["sc_out"] = po.ref_scale(ew, 0.37, -1.25)
+    bb = (rng.standard_normal(24) * 2).astype(np.float32)
+    bb[3] = 0.0  # division by zero gives 0 (binop_f32.glsl:27)
+    data["bin_b"] = bb
+    for op in range(4):
+        data[f"bin_out_op{op}"] = po.ref_binop(op, ew[:480], bb)  # src1 broadcast: i % 24
+    ne0, ne1, n_dims, n_seqs = 128, 3, 96, 2
+    rx = rng.standard_normal(ne0 * ne1 * n_seqs).astype(np.float32)
+    rp = np.array([7, 1234], np.int32)
+    data["rope_in"], data["rope_pos"] = rx, rp
+    data["rope_out"] = po.ref_rope_neox(rx, rp, ne0, ne1, n_dims, n_seqs, 10000.0 ** (-2.0 / n_dims), 1.0)
+    emb = rng.standard_normal((50, 40)).astype(np.float16)
+    eidx = np.array([0, 49, 7, -1, 50, 3, 3], np.int32)
+    data["emb_w"], data["emb_idx"] = emb, eidx
+    data["emb_out"] = po.ref_embedding(emb, eidx)
+
     out = Path(__file__).resolve().parent / "golden.npz"
     np.savez_compressed(out, **data)
     print(f"wrote {out} ({out.stat().st_size} bytes, {len(data)} arrays)")

@@ -13,6 +13,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -434,9 +435,10 @@ hipError_t hipPeekAtLastError(void) { return t_last; }
 //   mul_mat + f16:     (A, B, dst, K, N, -, M)  -> vkflame_dispatch_linear (TN)
 //   dequantize_*:      q4_0/q4_1/q5_0: (vx, y, int nb32); q8_0: (vx, y, int nb)
 //       or (vx, y, int64 k) when blockDim.x != 32; K-quants: (vx, y), nb = gridDim.x
-// Other names (activations, norms, rope, ...: not on this path) are logged
-// and skipped with hipSuccess, as the reference did (:849-851); with
-// VKFLAME_STRICT=1 they return hipErrorInvalidValue instead.
+//   unary ops, scale, rms_norm, rope, binary ops, softmax, get_rows: the
+//       reference's argument positions (:953-1095, :1190-1205), ggml_ops.cu.
+// Other names are logged and skipped with hipSuccess, as the reference did
+// (:849-851); with VKFLAME_STRICT=1 they return hipErrorInvalidValue instead.
 
 static int qtype_of(const std::string &n) {
     auto has = [&](const char *s) { return n.find(s) != std::string::npos; };
@@ -499,6 +501,87 @@ hipError_t hipLaunchKernel(const void *func, vkf_dim3 gridDim, vkf_dim3 blockDim
         default: nb = gridDim.x; break;
         }
         return from_vkf(vkflame_dispatch_dequant_async(ptr(0), ptr(1), nb, qt, stream));
+    }
+    // The rest of the table (shim/hip_runtime_shim.cpp:953-1095, 1190-1205),
+    // in the reference's order and argument positions.  Element counts that
+    // come from the launch grid are clamped to the destination's allocation
+    // when the allocation table knows it.
+    vkflame_set_stream(stream);
+    auto avail = [&](const void *p, uint64_t n, size_t es) {
+        void *base = nullptr;
+        size_t size = 0;
+        if (p && vkflame_ptr_lookup(p, &base, &size) == VKF_OK) {
+            const uint64_t left = ((uintptr_t)base + size - (uintptr_t)p) / es;
+            return std::min<uint64_t>(n, left);
+        }
+        return n;
+    };
+    auto f32 = [&](int i) { return *reinterpret_cast<float *>(args[i]); };
+    auto unary = [&](uint32_t op) {
+        const uint64_t n = avail(ptr(1), avail(ptr(0), (uint32_t)i32(2), 4), 4);
+        return from_vkf(vkflame_dispatch_elementwise_f32(nullptr, ptr(0), ptr(1), (uint32_t)n, op));
+    };
+    if (has("silu_f32") || has("silu")) return unary(VKF_EW_SILU);
+    if (has("gelu_quick") || has("gelu_erf") || has("gelu")) return unary(has("quick") ? VKF_EW_GELU_QUICK : VKF_EW_GELU_ERF);
+    if (has("relu")) return unary(VKF_EW_RELU);
+    if (has("tanh_f32") || (has("tanh") && !has("atanh"))) return unary(VKF_EW_TANH);
+    if (has("sigmoid")) return unary(VKF_EW_SIGMOID);
+    // sqrt before sqr: the reference tested "sqr" first, so sqrt kernels ran as sqr.
+    if (has("sqrt_f32") || has("sqrt")) return unary(VKF_EW_SQRT);
+    if (has("sqr_f32") || has("sqr")) return unary(VKF_EW_SQR);
+    if (has("neg_f32") || has("neg")) return unary(VKF_EW_NEG);
+    if (has("abs_f32") || has("abs")) return unary(VKF_EW_ABS);
+    if (has("scale_f32") || has("scale_f16")) {  // (x, dst, float scale, float bias, int64 n)
+        const uint64_t n = avail(ptr(1), avail(ptr(0), (uint64_t)i64(4), 4), 4);
+        return from_vkf(vkflame_dispatch_scale_f32(nullptr, ptr(0), ptr(1), (uint32_t)n, f32(2), f32(3)));
+    }
+    if (has("rms_norm_f32") || has("rms_norm")) {  // (x, dst, int ncols, ..., float eps at 6); rows = grid.x
+        return from_vkf(vkflame_dispatch_rms_norm_f32(nullptr, ptr(0), ptr(1), gridDim.x, (uint32_t)i32(2), f32(6)));
+    }
+    if (has("rope") && (has("neox") || has("llama") || has("norm"))) {
+        // (x, dst, ne0, ne1, s1, s2, n_dims, pos, freq_scale, ..., theta_scale at 13); sequences = grid.y
+        const uint32_t seqs = gridDim.y > 0 ? gridDim.y : 1;
+        return from_vkf(vkflame_dispatch_rope_neox(nullptr, ptr(0), ptr(7), ptr(1), (uint32_t)i32(2), (uint32_t)i32(3),
+                                                   (uint32_t)i32(6), seqs, f32(13), f32(8), 0, 0));
+    }
+    if (has("bin_bcast") || has("add_f32") || has("mul_f32") || has("sub_f32") || has("div_f32")) {
+        // (src0, src1, dst, ...): n = grid.x * block.x elements, no broadcast
+        const uint32_t op = has("mul") ? VKF_BINOP_MUL : has("sub") ? VKF_BINOP_SUB : has("div") ? VKF_BINOP_DIV
+                                                                                                 : VKF_BINOP_ADD;
+        uint64_t n = (uint64_t)gridDim.x * blockDim.x;
+        n = avail(ptr(2), avail(ptr(1), avail(ptr(0), n, 4), 4), 4);
+        return from_vkf(vkflame_dispatch_binop_f32(nullptr, ptr(0), ptr(1), ptr(2), (uint32_t)n, (uint32_t)n, op));
+    }
+    if (has("soft_max") || has("softmax")) {
+        // (x, mask, dst, ncols, ...) or the older (x, dst, ncols, ...): told
+        // apart by args[2] read as an int, as the reference did; rows = grid.y
+        const uint32_t rows = gridDim.y > 0 ? gridDim.y : 1;
+        int ncols = i32(2);
+        void *dst;
+        if (ncols > 0) {
+            dst = ptr(2);
+            ncols = i32(3);
+        } else {
+            dst = ptr(1);
+            ncols = i32(2);
+        }
+        if (ncols < 1) ncols = (int)blockDim.x;
+        return from_vkf(vkflame_dispatch_softmax(nullptr, ptr(0), dst, (int)rows, ncols));
+    }
+    if (has("get_rows") || has("getrows")) {
+        // (table [vocab x dim], int32 indices, fp32 dst, int dim); vocab and
+        // the row count from the allocation sizes (the reference's rule),
+        // the row count clamped to the destination's room.
+        const int dim = i32(3);
+        const bool f16 = has("f16");
+        void *base = nullptr;
+        size_t wsize = 0, isize = 0;
+        if (dim < 1 || vkflame_ptr_lookup(ptr(0), &base, &wsize) != VKF_OK) return ret(hipErrorInvalidValue);
+        const int V = (int)(((uintptr_t)base + wsize - (uintptr_t)ptr(0)) / ((size_t)dim * (f16 ? 2 : 4)));
+        if (vkflame_ptr_lookup(ptr(1), &base, &isize) != VKF_OK) return ret(hipErrorInvalidValue);
+        uint64_t B = ((uintptr_t)base + isize - (uintptr_t)ptr(1)) / 4;
+        B = avail(ptr(2), B * (uint64_t)dim, 4) / (uint64_t)dim;
+        return from_vkf(vkflame_get_rows(ptr(0), f16 ? 0 : 1, ptr(1), (float *)ptr(2), V, dim, (int)B, stream));
     }
     logf("hipLaunchKernel: unhandled kernel %s\n", name.c_str());
     return ret(strict() ? hipErrorInvalidValue : hipSuccess);

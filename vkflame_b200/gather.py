@@ -89,6 +89,24 @@ class GatherGroup:
         g.x_stride = x.stride if x is not None else 0
         return g
 
+    def chain_linear(self, W: int, wtype: int, K: int, n: int, out: GatheredBuffer | None = None,
+                     x_src: int = -1, x_plain: int = 0, y_plain: int = 0) -> "rt.ChainLinear":
+        """vkf_chain_linear_t of one link of a chain: this rank's n rows of W
+        (ggml blocks, K values each), writing its slice of `out` (gathered)
+        or, at world size 1, the plain fp16 row `y_plain`; reading the
+        gathered output of chain entry `x_src`, or the fp16 row `x_plain`."""
+        c = rt.ChainLinear()
+        c.W, c.wtype, c.K, c.N, c.x_src, c.x_plain = W, wtype, K, n, x_src, x_plain
+        c.y_plain = y_plain
+        if out is not None:
+            r0, _ = shard.row_range(out.N, self.world, self.rank)
+            if r0 != self.rank * n or out.N != n * self.world:
+                raise ValueError("shard rows do not match the gathered buffer")
+            for q in range(self.world):
+                c.y_rank[q] = out.ptrs[q] + (r0 // 2) * 8
+            c.y_stride = out.stride
+        return c
+
     def close(self) -> None:
         for base in self._opened.values():
             rt.ipc_close(base)

@@ -53,6 +53,11 @@ _SIGS = {
     "vkflame_linear_int8": ([C.c_void_p] * 7 + [C.c_int] * 4 + [C.c_void_p], C.c_int),
     "vkflame_quant_linear_gather": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                      C.c_int64, C.c_int64, C.c_uint, C.c_void_p, C.c_void_p], C.c_int),
+    "vkflame_chain_create": ([C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_uint, C.POINTER(C.c_void_p)], C.c_int),
+    "vkflame_chain_run": ([C.c_void_p, C.c_void_p], C.c_int),
+    "vkflame_chain_epoch": ([C.c_void_p, C.POINTER(C.c_int)], C.c_int),
+    "vkflame_chain_trace": ([C.c_void_p, C.c_void_p], C.c_int),
+    "vkflame_chain_destroy": ([C.c_void_p], C.c_int),
     "vkflame_ipc_handle": ([C.c_void_p, C.c_void_p, C.POINTER(C.c_uint64)], C.c_int),
     "vkflame_ipc_open": ([C.c_void_p, C.POINTER(C.c_void_p)], C.c_int),
     "vkflame_ipc_close": ([C.c_void_p], C.c_int),
@@ -152,6 +157,45 @@ def quant_linear_gather(W: int, wtype: int, X: int, ytype: int, M: int, N: int, 
                         flags: int, g: Gather, stream: int = 0) -> None:
     _check(lib().vkflame_quant_linear_gather(W, wtype, X, ytype, M, N, K, ldx, ldy, flags, C.byref(g), stream),
            "quant_linear_gather")
+
+
+class ChainLinear(C.Structure):
+    """vkf_chain_linear_t (include/vkflame_rt.h)."""
+    _fields_ = [("W", C.c_void_p), ("wtype", C.c_int), ("K", C.c_int), ("N", C.c_int), ("x_src", C.c_int),
+                ("x_plain", C.c_void_p), ("y_rank", C.c_void_p * MAX_RANKS), ("y_stride", C.c_int64),
+                ("y_plain", C.c_void_p)]
+
+
+CHAIN_TRACE = 1
+
+
+class Chain:
+    """A token's decode linears as one persistent kernel (vkflame_chain_*)."""
+
+    def __init__(self, linears: list, world: int = 1, rank: int = 0, flags: int = 0):
+        arr = (ChainLinear * len(linears))(*linears)
+        h = C.c_void_p()
+        _check(lib().vkflame_chain_create(arr, len(linears), world, rank, flags, C.byref(h)), "chain_create")
+        self.handle, self.n = h.value, len(linears)
+
+    def run(self, stream: int = 0) -> None:
+        _check(lib().vkflame_chain_run(self.handle, stream), "chain_run")
+
+    def epoch(self) -> int:
+        e = C.c_int()
+        _check(lib().vkflame_chain_epoch(self.handle, C.byref(e)), "chain_epoch")
+        return e.value
+
+    def trace(self):
+        import numpy as np
+        t = np.zeros((self.n, 2), np.uint64)
+        _check(lib().vkflame_chain_trace(self.handle, t.ctypes.data), "chain_trace")
+        return t
+
+    def close(self) -> None:
+        if self.handle:
+            _check(lib().vkflame_chain_destroy(self.handle), "chain_destroy")
+            self.handle = None
 
 
 def ipc_handle(ptr: int) -> tuple[bytes, int]:
