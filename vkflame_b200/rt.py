@@ -58,6 +58,17 @@ _SIGS = {
     "vkflame_chain_epoch": ([C.c_void_p, C.POINTER(C.c_int)], C.c_int),
     "vkflame_chain_trace": ([C.c_void_p, C.c_void_p], C.c_int),
     "vkflame_chain_destroy": ([C.c_void_p], C.c_int),
+    "vkflame_set_stream": ([C.c_void_p], C.c_int),
+    "vkflame_dispatch_elementwise_f32": ([C.c_void_p] * 3 + [C.c_uint32] * 2, C.c_int),
+    "vkflame_dispatch_scale_f32": ([C.c_void_p] * 3 + [C.c_uint32, C.c_float, C.c_float], C.c_int),
+    "vkflame_dispatch_binop_f32": ([C.c_void_p] * 4 + [C.c_uint32] * 3, C.c_int),
+    "vkflame_dispatch_rms_norm_f32": ([C.c_void_p] * 3 + [C.c_uint32] * 2 + [C.c_float], C.c_int),
+    "vkflame_dispatch_rms_norm": ([C.c_void_p] * 4 + [C.c_int] * 2 + [C.c_float], C.c_int),
+    "vkflame_dispatch_softmax": ([C.c_void_p] * 3 + [C.c_int] * 2, C.c_int),
+    "vkflame_dispatch_rope_neox": ([C.c_void_p] * 4 + [C.c_uint32] * 4 + [C.c_float] * 2 + [C.c_uint32] * 2,
+                                   C.c_int),
+    "vkflame_dispatch_embedding": ([C.c_void_p] * 4 + [C.c_int] * 3, C.c_int),
+    "vkflame_get_rows": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p] + [C.c_int] * 3 + [C.c_void_p], C.c_int),
     "vkflame_ipc_handle": ([C.c_void_p, C.c_void_p, C.POINTER(C.c_uint64)], C.c_int),
     "vkflame_ipc_open": ([C.c_void_p, C.POINTER(C.c_void_p)], C.c_int),
     "vkflame_ipc_close": ([C.c_void_p], C.c_int),
