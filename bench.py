@@ -477,7 +477,10 @@ def bench_stack(args, world, rank, local, dist):
 
 
 # ------------------------------------------------------- sub-benchmarks -----
-def graph_time(fn, iters=20):
+def graph_time(fn, iters=20, replays=5):
+    """Device time per call: `iters` calls captured in one CUDA graph,
+    replayed `replays` times after a warm-up replay (CUDA events on the
+    launching stream); the median replay."""
     import torch
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
@@ -490,19 +493,41 @@ def graph_time(fn, iters=20):
                 fn(s.cuda_stream)
         g.replay()
         torch.cuda.synchronize()
-        e0, e1 = timed_graph(g, s, 1)
-        torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / iters
+        times = []
+        for _ in range(replays):
+            e0, e1 = timed_graph(g, s, 1)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1) / iters)
+    return float(np.median(times))
 
 
-GEMV_CASES = {"config3_q4K_gate_up_M1": (S.Q4_K, 5120, 13824, 1),
-              "config3_q4K_gate_up_M8": (S.Q4_K, 5120, 13824, 8),
-              "config3_q4K_qo_M1": (S.Q4_K, 5120, 5120, 1),
-              "config3_q4K_down_M1": (S.Q4_K, 13824, 5120, 1),
-              "config1_q4_0_M1": (S.Q4_0, 4096, 4096, 1),
-              "config1_q4_0_M32": (S.Q4_0, 4096, 4096, 32),
-              "q8_0_gate_up_M1": (S.Q8_0, 5120, 13824, 1),
-              "q6K_down_M1": (S.Q6_K, 13824, 5120, 1)}
+def hbm_roofline(bytes_per_call, ms):
+    peaks = measured_peaks()
+    peak = peaks.get("hbm_gbs") or HBM_FALLBACK_GBS
+    a = bytes_per_call / (ms * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": a, "peak": peak, "unit": "GB/s", "frac": a / peak,
+            "peak_source": "of measured" if peaks.get("hbm_gbs") else "of fallback"}
+
+
+def tensor_roofline(ops_per_call, ms, kind):
+    """kind "f16": the measured cuBLAS bf16 burst; "i8": twice it (no int8
+    figure is measured; the dense int8 rate of B200 is twice its bf16 rate)."""
+    peaks = measured_peaks()
+    bf16 = peaks.get("bf16_tflops") or 1590.0
+    peak = bf16 * (2 if kind == "i8" else 1)
+    a = ops_per_call / (ms * 1e-3) / 1e12
+    return {"bound": "tensor", "achieved": a, "peak": peak, "unit": "TOPS" if kind == "i8" else "TFLOP/s",
+            "frac": a / peak, "peak_source": ("2 x measured bf16 burst (int8 assumption)" if kind == "i8" else
+                                             "measured bf16 burst") if peaks.get("bf16_tflops") else "fallback"}
+
+
+# Config 1 and 3 cases (K, N per BASELINE.json): name -> (format, K, N, M)
+GEMV_CASES = {f"config1_q4_0_M{m}": (S.Q4_0, 4096, 4096, m) for m in (1, 32)}
+for _shape, (_k, _n) in {"qo": (5120, 5120), "kv": (5120, 1024), "gate_up": (5120, 13824),
+                         "down": (13824, 5120)}.items():
+    for _m in (1, 2, 4, 8):
+        GEMV_CASES[f"config3_q4K_{_shape}_M{_m}"] = (S.Q4_K, _k, _n, _m)
+GEMV_CASES.update({"q8_0_gate_up_M1": (S.Q8_0, 5120, 13824, 1), "q6K_down_M1": (S.Q6_K, 13824, 5120, 1)})
 
 
 def bench_gemv_case(name, iters_per_copy=4):
@@ -525,23 +550,58 @@ def bench_gemv_case(name, iters_per_copy=4):
         rt.quant_linear_ex(w.data_ptr(), q, x.data_ptr(), rt.X_F16, y.data_ptr(), rt.Y_F16, M, N, K, K, N,
                            rt.FLAG_STATIC_WEIGHTS, sp)
     ms = graph_time(fn, iters=iters_per_copy * copies)
-    return {"us": ms * 1e3, "GB/s": (wb + M * K * 2 + M * N * 2) / (ms * 1e-3) / 1e9}
+    nbytes = wb + M * K * 2 + M * N * 2
+    return {"us": ms * 1e3, "GB/s": nbytes / (ms * 1e-3) / 1e9, "roofline": hbm_roofline(nbytes, ms),
+            "l2": f"weights rotated over {copies} copies ({copies * wb / 1e6:.0f} MB > 3x L2)"}
+
+
+def _lt(rt):
+    import ctypes as C
+    from vkflame_b200 import LIBS
+    lt = C.CDLL(str(LIBS["hipblaslt"]))
+    lt.hipblasLtMatrixLayoutCreate.argtypes = [C.POINTER(C.c_void_p), C.c_int, C.c_uint64, C.c_uint64, C.c_int64]
+    return lt
 
 
 def bench_int8_linear():
-    """Config 2: int8 linear with per-row / per-channel scales and bias (the
-    hipblasLt BIAS-epilogue call)."""
+    """Config 2 through the hipBLASLt drop-in, as the config states:
+    hipblasLtMatmul with int8 X (M x K) x int8 W (N x K, TRANSB = T),
+    per-row / per-channel scale pointers and the fp16 BIAS epilogue."""
+    import ctypes as C
     import torch
     from vkflame_b200 import rt
     M, N, K = 512, 11008, 4096
     xi = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
     wi = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda")
-    sx, sw = torch.rand(M, device="cuda") * 1e-2, torch.rand(N, device="cuda") * 1e-2
+    sx = torch.rand(M, device="cuda") * 9e-3 + 1e-3
+    sw = torch.rand(N, device="cuda") * 9e-3 + 1e-3
     bias = (torch.randn(N, device="cuda") * 0.02).half()
     yi = torch.empty((M, N), device="cuda", dtype=torch.float16)
-    ms = graph_time(lambda sp: rt.linear_int8(xi.data_ptr(), wi.data_ptr(), sx.data_ptr(), sw.data_ptr(),
-                                              bias.data_ptr(), yi.data_ptr(), 0, M, N, K, 0, sp))
-    return {"us": ms * 1e3, "TOPS": 2 * M * N * K / (ms * 1e-3) / 1e12}
+    lt = _lt(rt)
+    h, desc, la, lb, ld = (C.c_void_p() for _ in range(5))
+    assert lt.hipblasLtCreate(C.byref(h)) == 0 and lt.hipblasLtMatmulDescCreate(C.byref(desc), 0, 0) == 0
+    assert lt.hipblasLtMatrixLayoutCreate(C.byref(la), 2, M, K, K) == 0
+    assert lt.hipblasLtMatrixLayoutCreate(C.byref(lb), 2, N, K, K) == 0
+    assert lt.hipblasLtMatrixLayoutCreate(C.byref(ld), 0, M, N, N) == 0
+    def setattr_(attr, value, ctype):
+        v = ctype(value)
+        assert lt.hipblasLtMatmulDescSetAttribute(desc, attr, C.byref(v), C.sizeof(v)) == 0
+    setattr_(1, 112, C.c_int)                  # TRANSB = T
+    setattr_(5, 2, C.c_int)                    # EPILOGUE_BIAS
+    setattr_(6, bias.data_ptr(), C.c_void_p)   # BIAS_POINTER
+    setattr_(7, sx.data_ptr(), C.c_void_p)     # A_SCALE_POINTER (per row)
+    setattr_(8, sw.data_ptr(), C.c_void_p)     # B_SCALE_POINTER (per channel)
+    one, zero = C.c_float(1.0), C.c_float(0.0)
+    def fn(sp):
+        rc = lt.hipblasLtMatmul(h, desc, C.byref(one), C.c_void_p(xi.data_ptr()), la, C.c_void_p(wi.data_ptr()), lb,
+                                C.byref(zero), None, None, C.c_void_p(yi.data_ptr()), ld, None, None, C.c_size_t(0),
+                                C.c_void_p(sp))
+        assert rc == 0
+    ms = graph_time(fn, iters=20)
+    ops = 2 * M * N * K
+    return {"us": ms * 1e3, "TOPS": ops / (ms * 1e-3) / 1e12, "path": "hipblasLtMatmul (libhipblaslt.so.0)",
+            "roofline": tensor_roofline(ops, ms, "i8"),
+            "l2": "inputs 49 MB re-read from L2 between calls (fit in L2; tensor-bound)"}
 
 
 def bench_q8_prefill():
@@ -559,20 +619,104 @@ def bench_q8_prefill():
         # the activation quantiser and widening run (VKF_FLAG_STATIC_WEIGHTS)
         rt.quant_linear_ex(wq.data_ptr(), S.Q8_0, xq.data_ptr(), rt.X_Q8_1, yo.data_ptr(), rt.Y_F32, M, N, K,
                            K // 32, N, rt.FLAG_STATIC_WEIGHTS, sp)
-    ms = graph_time(c4, iters=5)
-    return {"us": ms * 1e3, "TOPS": 2 * M * N * K / (ms * 1e-3) / 1e12}
+    ms = graph_time(c4, iters=10)
+    ops = 2 * M * N * K
+    return {"us": ms * 1e3, "TOPS": ops / (ms * 1e-3) / 1e12, "roofline": tensor_roofline(ops, ms, "i8"),
+            "includes": "the on-device fp32 -> Q8_1 quantiser of X"}
+
+
+def bench_prefill_stack(M=512):
+    """Config 5 at M = 512: the 48-layer stack's 241 linears as a 512-token
+    prefill (vkflame_quant_linear_ex, tensor-core GEMMs), one CUDA graph per
+    step; 2 M N K flops summed over the linears."""
+    import torch
+    from vkflame_b200 import rt
+    links = stack_links()
+    xs = {K: torch.randn((M, K), device="cuda").half() for K in (HIDDEN, FFN)}
+    ys = {}
+    ws = []
+    flops = 0
+    for i, (name, q, K, N, inp) in enumerate(links):
+        ws.append(make_quant_weight_gpu(q, N, K, link_seed(0, i)))
+        ys.setdefault(N, torch.empty((M, N), device="cuda", dtype=torch.float16))
+        flops += 2 * M * N * K
+    def step(sp):
+        for i, (name, q, K, N, inp) in enumerate(links):
+            rt.quant_linear_ex(ws[i].data_ptr(), q, xs[K].data_ptr(), rt.X_F16, ys[N].data_ptr(), rt.Y_F16, M, N, K,
+                               K, N, rt.FLAG_STATIC_WEIGHTS, sp)
+    ms = graph_time(step, iters=1, replays=3)
+    wbytes = sum(w.numel() for w in ws)
+    del ws
+    torch.cuda.empty_cache()
+    return {"ms": ms, "TFLOP/s": flops / (ms * 1e-3) / 1e12, "tflop_per_step": flops / 1e12,
+            "weight_gb": wbytes / 1e9, "roofline": tensor_roofline(flops, ms, "f16"),
+            "note": "Q6_K links (attn_v, ffn_down, head) widen W to fp16 in scratch before the GEMM"}
 
 
 SUB_CASES = dict({n: (lambda n=n: bench_gemv_case(n)) for n in GEMV_CASES},
-                 config2_int8_linear_M512=bench_int8_linear, config4_q8_0_x_q8_1_M512=bench_q8_prefill)
+                 config2_int8_linear_M512=bench_int8_linear, config4_q8_0_x_q8_1_M512=bench_q8_prefill,
+                 config5_prefill_stack_M512=bench_prefill_stack)
 
 
 def sub_benchmarks(names=None):
-    """Configs 1-4 at one shape each (device time, CUDA graphs)."""
+    """Configs 1-4 at their shapes and config 5 at M = 512 (device time, CUDA graphs)."""
     from vkflame_b200 import rt
     out = {n: SUB_CASES[n]() for n in (names or SUB_CASES)}
     rt.check_kernel_errors()
     return out
+
+
+def cpu_baseline_int8(budget_s=3.0):
+    """Config 2 on the host: the oracle's int8 linear (int32 accumulators +
+    fp16 epilogue, OpenMP over rows) on a 32-row sample of the 512 x 4096 x
+    11008 problem, in TOPS."""
+    from oracle import pyoracle as po
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(1)
+    M, N, K = 32, 11008, 4096
+    x = rng.integers(-127, 128, (M, K), dtype=np.int8)
+    w = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    sx, sw = rng.uniform(1e-3, 1e-2, M).astype(np.float32), rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+    po.linear_int8(x[:2], w, sx[:2], sw, want_acc=False, threads=cores)
+    t0, reps = time.perf_counter(), 0
+    while time.perf_counter() - t0 < budget_s and reps < 50:
+        po.linear_int8(x, w, sx, sw, want_acc=False, threads=cores)
+        reps += 1
+    el = time.perf_counter() - t0
+    return {"value": 2 * M * N * K * reps / el / 1e12, "unit": "TOPS", "cores": cores, "kind": "port",
+            "sample": f"M=32 of 512 rows, N=11008, K=4096, {reps} reps ({el:.1f} s)"}
+
+
+def cpu_baseline_q8(budget_s=3.0):
+    """Config 4 on the host: the reference's mul_mat sequence (dequant Q8_0 W
+    and Q8_1 X to fp32, fp32 dot products) over a 1024-row, 32-token sample."""
+    from oracle import pyoracle as po
+    cores = os.cpu_count() or 1
+    M, N, K = 32, 1024, 5120
+    w = S.quant_matrix(S.Q8_0, N, K, seed=3)
+    xq = po.quantize_q8_1(S.normal_f32((M, K), seed=4))
+    po.quant_linear(S.Q8_0, w, xq, M, N, K, xtype=1, ytype=0, threads=cores)
+    t0, reps = time.perf_counter(), 0
+    while time.perf_counter() - t0 < budget_s and reps < 50:
+        po.quant_linear(S.Q8_0, w, xq, M, N, K, xtype=1, ytype=0, threads=cores)
+        reps += 1
+    el = time.perf_counter() - t0
+    return {"value": 2 * M * N * K * reps / el / 1e12, "unit": "TOPS", "cores": cores, "kind": "port",
+            "sample": f"M=32 of 512 rows, N=1024 of 13824, K=5120, {reps} reps ({el:.1f} s)"}
+
+
+def config_cpu_baselines(configs: dict) -> None:
+    """Attaches a bounded host baseline (the oracle's restatement of the
+    reference pipeline, all host cores) to each measured config entry."""
+    for name, c in configs.items():
+        if name in GEMV_CASES:
+            q, K, N, M = GEMV_CASES[name]
+            if M in (1, 32) or name.endswith("_M8"):
+                c["cpu_baseline"] = cpu_baseline_gemv(q, N, K, M, budget_s=1.5)
+        elif name.startswith("config2"):
+            c["cpu_baseline"] = cpu_baseline_int8()
+        elif name.startswith("config4"):
+            c["cpu_baseline"] = cpu_baseline_q8()
 
 
 def cpu_baseline_stack(budget_s=12.0):
@@ -645,6 +789,8 @@ def main():
             line["configs"] = sub_benchmarks()
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_stack()
+            if "configs" in line:
+                config_cpu_baselines(line["configs"])
     if rank == 0:
         print(json.dumps(line))
     if dist is not None:

@@ -163,6 +163,68 @@ def test_hip_launch_dequant_q8_0_int64_count(hip):
     assert np.array_equal(dst.get(np.float32).view(np.uint32), po.dequant(S.Q8_0, raw, nb).view(np.uint32))
 
 
+@pytest.mark.parametrize("q,name", [(S.Q4_0, "dequantize_block_q4_0<float>"), (S.Q4_1, "dequantize_block_q4_1"),
+                                    (S.Q5_0, "dequantize_block_q5_0<float>")])
+def test_hip_launch_dequant_nb32_convention(hip, q, name):
+    """q4_0 / q4_1 / q5_0: (vx, y, int nb32), nb32 = the count of 32-value
+    blocks (shim/hip_runtime_shim.cpp:896-920); the launch grid is ignored."""
+    raw = S.quant_matrix(q, 3, 512, seed=20 + q).ravel()
+    nb = raw.size // S.BLOCK_BYTES[q]
+    src, dst = Dev(hip, raw), Dev(hip, nbytes=nb * 32 * 4)
+    fn = register(hip, name)
+    assert launch(hip, fn, ((nb + 7) // 8, 1, 1), (32, 1, 1), [src.ptr, dst.ptr, (C.c_int, nb)]) == 0
+    assert np.array_equal(dst.get(np.float32).view(np.uint32), po.dequant(q, raw, nb).view(np.uint32))
+
+
+@pytest.mark.parametrize("q,name", [(S.Q5_K, "dequantize_block_q5_K<__half>"), (S.Q6_K, "dequantize_block_q6_K")])
+def test_hip_launch_dequant_k_quants_grid_count(hip, q, name):
+    """K-quants: (vx, y), one super-block per grid.x."""
+    raw = S.quant_matrix(q, 2, 1024, seed=30 + q).ravel()
+    nb = raw.size // S.BLOCK_BYTES[q]
+    src, dst = Dev(hip, raw), Dev(hip, nbytes=nb * 256 * 4)
+    fn = register(hip, name)
+    assert launch(hip, fn, (nb, 1, 1), (64, 1, 1), [src.ptr, dst.ptr]) == 0
+    assert np.array_equal(dst.get(np.float32).view(np.uint32), po.dequant(q, raw, nb).view(np.uint32))
+
+
+@pytest.mark.parametrize("M", [1, 40])
+@pytest.mark.parametrize("q,name", [(S.Q8_0, "mul_mat_q8_0_q8_1"), (S.Q6_K, "mul_mat_q6_K_q8_1"),
+                                    (S.Q4_0, "mul_mat_q4_0_q8_1"), (S.Q4_1, "mul_mat_q4_1_q8_1"),
+                                    (S.Q5_0, "mul_mat_q5_0_q8_1"), (S.Q5_K, "mul_mat_q5_K_q8_1")])
+def test_hip_launch_mul_mat_formats(hip, q, name, M):
+    """Every weight format of the mul_mat branch (shim/hip_runtime_shim.cpp:
+    1102-1166), Q4_1 and Q5_0 included (dequant + tensor-core GEMM)."""
+    N, K = 192, 1024
+    w = S.quant_matrix(q, N, K, seed=50 + q)
+    xq = po.quantize_q8_1(S.normal_f32((M, K), seed=51))
+    wd, xd, yd = Dev(hip, w), Dev(hip, xq), Dev(hip, nbytes=M * N * 4)
+    fn = register(hip, name)
+    args = [wd.ptr, xd.ptr, yd.ptr, (C.c_int, K), (C.c_int, N), (C.c_int, K), (C.c_int, M), (C.c_int, N)]
+    assert launch(hip, fn, (1, 1, 1), (32, 1, 1), args) == 0
+    y = yd.get(np.float32, (M, N)).astype(np.float64)
+    wf = po.dequant(q, w, N * K // S.BLOCK_VALUES[q]).reshape(N, K).astype(np.float64)
+    xf = po.dequant(S.Q8_1, xq, M * K // 32).reshape(M, K).astype(np.float64)
+    ref = xf @ wf.T
+    assert np.abs(y - ref).max() / np.abs(ref).max() < 2e-3
+
+
+def test_hip_launch_mul_mat_f16(hip):
+    """The fp16 mul_mat branch: (A = activations M x K, B = weights N x K,
+    dst fp16 M x N), K = args[3], N = args[4], M = args[6]
+    (shim/hip_runtime_shim.cpp:1174-1188, vkflame_dispatch_linear TN)."""
+    M, N, K = 24, 200, 320
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    w = rng.standard_normal((N, K)).astype(np.float16)
+    xd, wd, yd = Dev(hip, x), Dev(hip, w), Dev(hip, nbytes=M * N * 2)
+    fn = register(hip, "mul_mat_f16")
+    args = [xd.ptr, wd.ptr, yd.ptr, (C.c_int, K), (C.c_int, N), (C.c_int, K), (C.c_int, M)]
+    assert launch(hip, fn, (1, 1, 1), (32, 1, 1), args) == 0
+    got = yd.get(np.float16, (M, N)).astype(np.float64)
+    ref = x.astype(np.float64) @ w.astype(np.float64).T
+    assert np.abs(got - ref).max() / np.abs(ref).max() < 2e-3
+
+
 @pytest.mark.parametrize("M", [1, 40])
 def test_hip_launch_mul_mat_q4_K_q8_1(hip, M):
     """ggml's quantised mul_mat: weights Q4_K, activations Q8_1, fp32 output."""
@@ -255,6 +317,50 @@ def test_hipblas_k_zero_scales_c(hip, blas):
     assert np.array_equal(Cd.get(np.float32, (n, m)), c0 * np.float32(0.5))
 
 
+def test_hipblas_sgemm_fp32_accuracy(hip, blas):
+    """hipblasSgemm at fp32 accuracy (three tf32 products), with alpha, beta."""
+    m, n, k = 200, 136, 1000
+    rng = np.random.default_rng(12)
+    A = rng.standard_normal((m, k)).astype(np.float32)  # op N
+    B = rng.standard_normal((k, n)).astype(np.float32)  # op N
+    c0 = rng.standard_normal((m, n)).astype(np.float32)
+    Ad, Bd, Cd = Dev(hip, colmajor(A).T.copy()), Dev(hip, colmajor(B).T.copy()), Dev(hip, colmajor(c0).T.copy())
+    al, be = C.c_float(0.75), C.c_float(-0.5)
+    assert blas.hipblasSgemm(blas.handle, OP_N, OP_N, m, n, k, C.byref(al), C.c_void_p(Ad.ptr), m, C.c_void_p(Bd.ptr),
+                             k, C.byref(be), C.c_void_p(Cd.ptr), m) == 0
+    got = Cd.get(np.float32, (n, m)).T.astype(np.float64)
+    ref = 0.75 * A.astype(np.float64) @ B.astype(np.float64) - 0.5 * c0.astype(np.float64)
+    # fp32 class: a k = 1000 fp32 dot product is good to ~1e-6 of its scale;
+    # one tf32 product would be ~1e-3
+    assert np.abs(got - ref).max() / np.abs(ref).max() < 2e-5
+
+
+def test_hipblas_batched_pointer_arrays(hip, blas):
+    """Sgemm/HgemmBatched with device arrays of device pointers."""
+    m, n, k, batch = 64, 40, 96, 3
+    rng = np.random.default_rng(13)
+    for half in (False, True):
+        dt = np.float16 if half else np.float32
+        As = [rng.standard_normal((k, m)).astype(dt) for _ in range(batch)]  # op T: stored k x m col-major
+        Bs = [rng.standard_normal((k, n)).astype(dt) for _ in range(batch)]
+        Ad = [Dev(hip, a.T.copy()) for a in As]
+        Bd = [Dev(hip, b.T.copy()) for b in Bs]
+        Cd = [Dev(hip, nbytes=m * n * np.dtype(dt).itemsize) for _ in range(batch)]
+        arrs = [Dev(hip, np.array([d.ptr for d in L], np.uint64)) for L in (Ad, Bd, Cd)]
+        if half:
+            one, zero = C.c_uint16(int(np.float16(1).view(np.uint16))), C.c_uint16(0)
+            fn = blas.hipblasHgemmBatched
+        else:
+            one, zero = C.c_float(1.0), C.c_float(0.0)
+            fn = blas.hipblasSgemmBatched
+        assert fn(blas.handle, OP_T, OP_N, m, n, k, C.byref(one), C.c_void_p(arrs[0].ptr), k, C.c_void_p(arrs[1].ptr), k,
+                  C.byref(zero), C.c_void_p(arrs[2].ptr), m, batch) == 0
+        for i in range(batch):
+            got = Cd[i].get(dt, (n, m)).T.astype(np.float64)
+            ref = As[i].T.astype(np.float64) @ Bs[i].astype(np.float64)
+            assert np.abs(got - ref).max() / np.abs(ref).max() < 2e-3
+
+
 def test_hipblas_sgemm_tf32(hip, blas):
     m, n, k = 128, 64, 256
     rng = np.random.default_rng(2)
@@ -266,7 +372,7 @@ def test_hipblas_sgemm_tf32(hip, blas):
                              k, C.byref(zero), C.c_void_p(Cd.ptr), m) == 0
     got = Cd.get(np.float32, (n, m)).T.astype(np.float64)
     ref = A.T.astype(np.float64) @ B.astype(np.float64)
-    assert np.abs(got - ref).max() / np.abs(ref).max() < 2e-3  # tf32 products
+    assert np.abs(got - ref).max() / np.abs(ref).max() < 2e-5  # three tf32 products: fp32 accuracy
 
 
 def test_hipblas_gemmex_int8_int32(hip, blas):

@@ -32,6 +32,8 @@ int gemm_tf32_tn(const float *A, int64_t lda, const float *B, int64_t ldb, int M
 int transpose(const void *src, int64_t lds, void *dst, int64_t ldd, int rows, int cols, int esize,
               cudaStream_t stream);
 int scale_c(void *C, int ctype, int64_t ldc, int m, int n, float beta, cudaStream_t stream);
+int split_tf32(const float *src, int64_t lds, float *hi, float *lo, int64_t ldd, int rows, int k,
+               cudaStream_t stream);
 
 
 static int esize_of(int t) { return t == BT_F16 ? 2 : t == BT_I8 ? 1 : 4; }
@@ -75,10 +77,12 @@ int blas_gemm_ex(int transA, int transB, int m, int n, int k, float alpha, const
     if (lda < (transA ? k : m) || ldb < (transB ? n : k)) return VKF_ERR_INVALID;
     const int es = esize_of(atype);
     const int64_t kp = ((int64_t)k * es + 15) / 16 * 16 / es;
-    // Staging regions: A'' (n rows, from B) first, then B'' (m rows, from A).
+    // Staging regions: A'' (n rows, from B) first, then B'' (m rows, from A);
+    // fp32 output from fp32 operands adds the tf32 hi/lo halves of both.
     const size_t a2bytes = ((size_t)n * kp * es + 255) & ~size_t(255);
     const size_t b2bytes = ((size_t)m * kp * es + 255) & ~size_t(255);
-    uint8_t *scr = (uint8_t *)stream_scratch(stream, a2bytes + b2bytes);
+    const bool split = atype == BT_F32 && ctype == BT_F32;
+    uint8_t *scr = (uint8_t *)stream_scratch(stream, (a2bytes + b2bytes) * (split ? 3 : 1));
     if (!scr) return VKF_ERR_NOMEM;
     // A'' (n x k) from B: K-major iff op(B) = B (column-major k x n = row-major n x k).
     const void *a2, *b2;
@@ -88,6 +92,24 @@ int blas_gemm_ex(int transA, int transB, int m, int n, int k, float alpha, const
     // B'' (m x k) from A: K-major iff op(A) = A^T (column-major k x m = row-major m x k).
     rc = prepare(A, lda, m, k, es, transA, scr + a2bytes, &b2, &ldb2, stream);
     if (rc) return rc;
+    if (split) {
+        // fp32 GEMM as three tf32 products (hipblasSgemm callers expect fp32
+        // accuracy, not tf32's 10-bit mantissa): x = hi + lo per operand,
+        // C = a(lo_A' hi_B') + bC, then += a(hi_A' lo_B'), then += a(hi_A' hi_B')
+        // with the epilogue (bias, activation) on the last pass; lo x lo
+        // (~2^-22 relative) is dropped.
+        float *ah = (float *)(scr + a2bytes + b2bytes), *al = (float *)((uint8_t *)ah + a2bytes);
+        float *bh = (float *)((uint8_t *)al + a2bytes), *bl = (float *)((uint8_t *)bh + b2bytes);
+        if ((rc = split_tf32((const float *)a2, lda2, ah, al, kp, n, k, stream))) return rc;
+        if ((rc = split_tf32((const float *)b2, ldb2, bh, bl, kp, m, k, stream))) return rc;
+        if (row_scale || col_scale) return VKF_ERR_UNSUPPORTED;
+        if ((rc = gemm_tf32_tn(al, kp, bh, kp, n, m, k, alpha, beta, beta != 0.0f ? C : nullptr, ldc, 0, nullptr, 0,
+                               C, ldc, 0, stream)))
+            return rc;
+        if ((rc = gemm_tf32_tn(ah, kp, bl, kp, n, m, k, alpha, 1.0f, C, ldc, 0, nullptr, 0, C, ldc, 0, stream)))
+            return rc;
+        return gemm_tf32_tn(ah, kp, bh, kp, n, m, k, alpha, 1.0f, C, ldc, 0, bias, act, C, ldc, 0, stream);
+    }
     const int y_f16 = ctype == BT_F16;
     if (atype == BT_I8) {
         if (alpha != 1.0f || beta != 0.0f) return VKF_ERR_UNSUPPORTED;

@@ -45,7 +45,33 @@ __global__ void __launch_bounds__(256) scale_kernel(T *C, int64_t ldc, int m, in
     }
 }
 
+// x = hi + lo with hi = x rounded to tf32 (10-bit mantissa, ties away) and
+// lo = x - hi (exact in fp32); both K-major rows x k, row stride ldd.
+__global__ void __launch_bounds__(256) split_tf32_kernel(const float *__restrict__ src, int64_t lds,
+                                                         float *__restrict__ hi, float *__restrict__ lo, int64_t ldd,
+                                                         int rows, int k) {
+    const int64_t total = (int64_t)rows * k;
+    for (int64_t e = blockIdx.x * 256ll + threadIdx.x; e < total; e += (int64_t)gridDim.x * 256) {
+        const int64_t r = e / k, c = e - r * k;
+        const float x = src[r * lds + c];
+        uint32_t h;
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+        const float hf = __uint_as_float(h);
+        hi[r * ldd + c] = hf;
+        lo[r * ldd + c] = x - hf;
+    }
+}
+
 }  // namespace
+
+int split_tf32(const float *src, int64_t lds, float *hi, float *lo, int64_t ldd, int rows, int k,
+               cudaStream_t stream) {
+    if (rows <= 0 || k <= 0) return VKF_OK;
+    const int64_t total = (int64_t)rows * k;
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+    split_tf32_kernel<<<grid, 256, 0, stream>>>(src, lds, hi, lo, ldd, rows, k);
+    return check_launch();
+}
 
 // hipBLAS GEMM with k == 0: C = beta * C (column-major m x n, ldc).
 int scale_c(void *C, int ctype, int64_t ldc, int m, int n, float beta, cudaStream_t stream) {

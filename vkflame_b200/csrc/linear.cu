@@ -146,9 +146,15 @@ static int quant_linear_gemv(const void *W, int wtype, const void *X, int xtype,
     return VKF_OK;
 }
 
+// Formats with no fused decoder (Q4_1, Q5_0): widened to fp16 by their
+// bit-exact dequant kernel, then the tensor-core GEMM, at every M (the
+// reference's dequant + GEMM chain, shim/hip_runtime_shim.cpp:1129-1166,
+// with one fp16 rounding of each weight).
+static bool widen_format(int wtype) { return wtype == VKF_DEQUANT_Q4_1 || wtype == VKF_DEQUANT_Q5_0; }
+
 int quant_linear(const void *W, int wtype, const void *X, int xtype, void *Y, int ytype, int M, int N, int K,
                  int64_t ldx, int64_t ldy, cudaStream_t stream, unsigned flags) {
-    if (!gemv_format(wtype)) return VKF_ERR_UNSUPPORTED;
+    if (!gemv_format(wtype) && !widen_format(wtype)) return VKF_ERR_UNSUPPORTED;
     if (M < 0 || N < 0 || K < 0 || (xtype != VKF_X_F16 && xtype != VKF_X_Q8_1) ||
         (ytype != VKF_Y_F32 && ytype != VKF_Y_F16))
         return VKF_ERR_INVALID;
@@ -168,7 +174,8 @@ int quant_linear(const void *W, int wtype, const void *X, int xtype, void *Y, in
     if ((wtype == VKF_DEQUANT_Q4_K || wtype == VKF_DEQUANT_Q5_K) ? (wa & 3) : (wa & 1)) return VKF_ERR_BADPTR;
     if ((uintptr_t)Y & (ytype == VKF_Y_F16 ? 1 : 3)) return VKF_ERR_BADPTR;
     if (xtype == VKF_X_F16 && ((uintptr_t)X & 1)) return VKF_ERR_BADPTR;
-    if (M > gemv_max_m()) return quant_linear_gemm(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, stream, flags);
+    if (M > gemv_max_m() || widen_format(wtype))
+        return quant_linear_gemm(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, stream, flags);
     return quant_linear_gemv(W, wtype, X, xtype, Y, ytype, M, N, K, ldx, ldy, stream, flags);
 }
 
