@@ -153,6 +153,11 @@ def test_quant_linear_prefill_q8_1(rt):
     (S.Q5_K, 64, 256, 5120, False, 264),    # 14B K, padded output rows
     (S.Q4_0, 129, 384, 4096, True, 384),    # 129 -> activation tiles of 256
     (S.Q4_K, 96, 1000, 1280, True, 1000),   # 128-wide activation tile, odd N
+    # Q6_K: 210-byte super-blocks, rows fetched one bulk copy each from the
+    # 16-byte boundary below them (row starts at every even offset mod 16)
+    (S.Q6_K, 300, 200, 2048, True, 256),    # ragged tiles, padded output rows
+    (S.Q6_K, 512, 640, 13824, False, 640),  # ffn_down K (row pitch 11340 = 12 mod 16)
+    (S.Q6_K, 40, 1000, 5120, True, 1000),   # attn_v / head K (pitch 4200 = 8 mod 16), odd N
 ])
 def test_quant_linear_prefill_fused_shapes(rt, q, M, N, K, f16, ldy):
     """Fused-dequant tcgen05 prefill (packed W bytes -> fp16 tiles in shared

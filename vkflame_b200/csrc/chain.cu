@@ -342,18 +342,28 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
                     const int which = tb == first_tile ? 0 : 1;
                     float *wsp = L.ws + ((int64_t)cta * 2 + which) * 16;
                     if (lane < 16) wsp[lane] = v;
-                    const int c_first = cta_of_item(tb * L.S, L.I, G), c_last = cta_of_item((tb + 1) * L.S - 1, L.I, G);
+                    // The tile's contributors are the owners of its S items (with
+                    // fewer items than CTAs, CTAs between them may own none).
+                    int owners = 0;
+                    for (int i = tb * L.S, prev = -1; i < (tb + 1) * L.S; ++i) {
+                        const int c = cta_of_item(i, L.I, G);
+                        owners += c != prev;
+                        prev = c;
+                    }
                     __syncwarp();
                     int fin = 0;
                     if (lane == 0) {
                         __threadfence();
-                        fin = atomicAdd(&L.cnt[tb], 1) == c_last - c_first;
+                        fin = atomicAdd(&L.cnt[tb], 1) == owners - 1;
                         if (fin) __threadfence();
                     }
                     if (__shfl_sync(0xffffffffu, fin, 0)) {
                         float t = 0.f;
                         if (lane < 16)
-                            for (int c = c_first; c <= c_last; ++c) {
+                            for (int i = tb * L.S, prev = -1; i < (tb + 1) * L.S; ++i) {
+                                const int c = cta_of_item(i, L.I, G);
+                                if (c == prev) continue;
+                                prev = c;
                                 const int wc = tb == first_item(c, L.I, G) / L.S ? 0 : 1;
                                 t += __ldcg(L.ws + ((int64_t)c * 2 + wc) * 16 + lane);
                             }

@@ -76,6 +76,15 @@ template <> struct Packed<VKF_DEQUANT_Q4_0> { static constexpr int RB = 8 * 18; 
 template <> struct Packed<VKF_DEQUANT_Q8_0> { static constexpr int RB = 8 * 34; };
 template <> struct Packed<VKF_DEQUANT_Q4_K> { static constexpr int RB = 144; };
 template <> struct Packed<VKF_DEQUANT_Q5_K> { static constexpr int RB = 176; };
+// Q6_K: 210 packed bytes per row and 256 values, so row pitches are not
+// 16-byte multiples and no tensor map describes the rows.  Each row's 210
+// bytes are fetched with its own bulk copy from the 16-byte boundary below
+// them (at most 224 bytes) into a 240-byte slot (15 granules: odd, so eight
+// consecutive rows' 16-byte loads hit eight distinct bank groups); the
+// converter reads the row at the slot + its start's offset mod 16.
+template <> struct Packed<VKF_DEQUANT_Q6_K> { static constexpr int RB = 240; };
+template <int QT> constexpr bool row_copies() { return QT == VKF_DEQUANT_Q6_K; }
+constexpr int Q6_ROW = 210;
 
 #ifdef VKF_QGEMM_TIMING
 // Cycle accumulators per CTA: [0] converter raw wait, [1] converter empty
@@ -100,6 +109,8 @@ struct Params {
     float *ws;        // per CTA: [NB*BX/4][128][4] fp32 partials (4-column groups)
     int *flags;       // [grid] partial published (reset by the consumer)
     unsigned *err;
+    const uint8_t *W; // the ggml rows (row-copy formats)
+    int64_t row_bytes;
 };
 
 // Segment walk shared by every role: CTA c owns units [u0, u1); a segment is
@@ -299,6 +310,53 @@ __device__ __forceinline__ void convert32(const uint8_t *rp, uint32_t (&o)[16]) 
     }
 }
 
+// 32 bytes at (even) byte offset p of a shared-memory row slot (16-byte
+// aligned): three aligned 16-byte loads, then the words selected and shifted
+// by p's offset within its granule (2-byte granularity).
+__device__ __forceinline__ void lds32_at(const uint8_t *slot, int p, uint32_t (&out)[8]) {
+    const uint8_t *b = slot + (p & ~15);
+    const uint4 a0 = *reinterpret_cast<const uint4 *>(b), a1 = *reinterpret_cast<const uint4 *>(b + 16),
+                a2 = *reinterpret_cast<const uint4 *>(b + 32);
+    const uint32_t w[12] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w, a2.x, a2.y, a2.z, a2.w};
+    const int ws = (p >> 2) & 3;
+    const uint32_t sh = (uint32_t)(p & 3) * 8;
+    uint32_t v[9];
+#pragma unroll
+    for (int j = 0; j < 9; ++j) v[j] = ws == 0 ? w[j] : ws == 1 ? w[j + 1] : ws == 2 ? w[j + 2] : w[j + 3];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[j] = __funnelshift_r(v[j], v[j + 1], sh);
+}
+
+// Q6_K (dequant_q6_k.glsl:28-58), the 32 values of sub-block B (ip = B / 4,
+// s = B % 4): code q = nibble of ql[64 ip + 32 (s & 1) + l] (low for s < 2)
+// | bits 2s, 2s + 1 of qh[32 ip + l] << 4; value = d * float(sc * (q - 32))
+// with sc = scales[8 ip + 2 s + l / 16].  sc * (q - 32) is an exact integer
+// and its product with the fp16 d is exact in fp32 (24 bits), so the one
+// rounding is to fp16: the shader's value rounded once.  row: the row's slot;
+// off: the row's first byte within it.
+template <int B>
+__device__ __forceinline__ void convert32_q6(const uint8_t *row, int off, uint32_t (&o)[16]) {
+    constexpr int IP = B / 4, S = B % 4;
+    uint32_t ql[8], qh[8];
+    lds32_at(row, off + 64 * IP + 32 * (S & 1), ql);
+    lds32_at(row, off + 128 + 32 * IP, qh);
+    const uint32_t scw = *reinterpret_cast<const uint16_t *>(row + off + 192 + 8 * IP + 2 * S);
+    const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(row + off + 208)));
+    const float sc0 = (float)(int8_t)(scw & 0xFF), sc1 = (float)(int8_t)(scw >> 8);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t nib = (S >= 2 ? ql[j] >> 4 : ql[j]) & 0x0F0F0F0Fu;
+        const uint32_t c = nib | (((qh[j] >> (2 * S)) & 0x03030303u) << 4);
+        const float sc = j < 4 ? sc0 : sc1;
+        float f[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)  // 2^23 + code, exact; minus 2^23 + 32: code - 32, exact
+            f[e] = d * (sc * (__uint_as_float(__byte_perm(c, 0x4B000000u, 0x7650u | e)) - 8388640.0f));
+        o[2 * j] = h2u(__floats2half2_rn(f[0], f[1]));
+        o[2 * j + 1] = h2u(__floats2half2_rn(f[2], f[3]));
+    }
+}
+
 // Row (within a group of 8) served by lane group g = lane >> 2, ordered so
 // that each 8-lane store phase writes 8 distinct 16-byte bank groups of the
 // swizzled tile: chunk sets {2cp} (Q8_0) pair rows r, r^1; {cp} (K-quants)
@@ -432,7 +490,43 @@ __global__ void __launch_bounds__(NT, 1)
     } else if (warp == W_RAW) {
         // ---- packed weight bytes: one tensor copy per 128 rows x 256 values ----
         if (!p.prefetch) asm volatile("griddepcontrol.wait;" ::: "memory");
-        if (lane == 0) {
+        if constexpr (row_copies<QT>()) {
+            // one bulk copy per row (4 rows per lane), 16-byte aligned source
+            // and size; the transaction count is the warp's byte total
+            int g = 0;
+            bool ok = true;
+            for (int u = u_begin; u < u_end && ok;) {
+                const Seg sg = seg_at(u);
+                u += sg.kr1 - sg.kr0;
+                const int n0 = (sg.tile / x_tiles) * BW;
+                for (int kr = sg.kr0; kr < sg.kr1; ++kr, ++g) {
+                    const int s = g % RS;
+                    if (g >= RS && !(ok = mbar_wait(&raw_empty[s], ((g / RS) & 1) ^ 1, p.err))) break;
+                    const uint8_t *src[4];
+                    uint32_t sz[4], total = 0;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int r = lane + 32 * i;
+                        sz[i] = 0;
+                        src[i] = nullptr;
+                        if (n0 + r < p.N) {
+                            const uint8_t *q = p.W + (int64_t)(n0 + r) * p.row_bytes + (int64_t)kr * Q6_ROW;
+                            const uint32_t mis = (uint32_t)((uintptr_t)q & 15);
+                            src[i] = q - mis;
+                            sz[i] = (mis + Q6_ROW + 15) & ~15u;
+                            total += sz[i];
+                        }
+                    }
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+                    if (lane == 0) mbar_arrive_expect_tx(&raw_full[s], total);
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if (sz[i]) bulk_g2s(raw + s * RAW_BYTES + (lane + 32 * i) * RB, src[i], sz[i], &raw_full[s]);
+                }
+            }
+        } else if (lane == 0) {
             int g = 0;
             bool ok = true;
             for (int u = u_begin; u < u_end && ok;) {
@@ -464,6 +558,12 @@ __global__ void __launch_bounds__(NT, 1)
                 QT_ACC(0);
             }
             const uint8_t *rp = raw + rs * RAW_BYTES + row * RB;
+            int roff = 0;  // row-copy formats: the row's first byte within its slot
+            if constexpr (row_copies<QT>()) {
+                const int tile = u / KR, kr = u - tile * KR;
+                const int64_t n = (int64_t)(tile / x_tiles) * BW + row;
+                roff = (int)((uintptr_t)(p.W + n * p.row_bytes + (int64_t)kr * Q6_ROW) & 15);
+            }
             auto kblock = [&](auto kk_c) {
                 constexpr int KK = decltype(kk_c)::value;
                 const int s = g % NS;
@@ -476,8 +576,13 @@ __global__ void __launch_bounds__(NT, 1)
                     QT_T0;
                     tc::fence_after_sync();  // the MMAs that read this TMEM stage are complete
                     uint32_t o[16];
-                    if (h == 0) convert32<QT, 2 * KK>(rp, o);
-                    else convert32<QT, 2 * KK + 1>(rp, o);
+                    if constexpr (row_copies<QT>()) {
+                        if (h == 0) convert32_q6<2 * KK>(rp, roff, o);
+                        else convert32_q6<2 * KK + 1>(rp, roff, o);
+                    } else {
+                        if (h == 0) convert32<QT, 2 * KK>(rp, o);
+                        else convert32<QT, 2 * KK + 1>(rp, o);
+                    }
                     tc::tmem_st16(ta0 + 32 * s, o);
                     tc::tmem_wait_st();
                     tc::fence_before_sync();
@@ -494,7 +599,7 @@ __global__ void __launch_bounds__(NT, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&raw_empty[rs]);
         }
-    } else if (warp >= W_CONV) {
+    } else if (warp >= W_CONV && !row_copies<QT>()) {
         // ---- converters: warp cw owns rows 16 cw .. 16 cw + 15 ----
         const int cw = warp - W_CONV;
         const int cp = lane & 3;
@@ -789,9 +894,11 @@ static int launch(const void *W, const void *X, int64_t ldx, void *Y, int y_f16,
     using C = Cfg<QT, BX, NB, ATM>;
     static_assert(C::FITS, "ring does not fit shared memory");
     constexpr int NC = BX * NB;
-    const int64_t row_bytes = (int64_t)K / RV * C::RB;
+    const int64_t row_bytes = (int64_t)K / RV * (row_copies<QT>() ? Q6_ROW : C::RB);
     CUtensorMap tx, tw;
-    if (!make_kmajor_map(&tx, X, 2, M, K, ldx, BX) || !make_byte_matrix_map(&tw, W, N, row_bytes, C::RB, BW))
+    memset(&tw, 0, sizeof(tw));
+    if (!make_kmajor_map(&tx, X, 2, M, K, ldx, BX) ||
+        (!row_copies<QT>() && !make_byte_matrix_map(&tw, W, N, row_bytes, C::RB, BW)))
         return VKF_ERR_UNSUPPORTED;
     auto kern = qgemm_kernel<QT, BX, NB, C::NS, C::RS, ATM>;
     static bool attr[64] = {false};
@@ -814,7 +921,7 @@ static int launch(const void *W, const void *X, int64_t ldx, void *Y, int y_f16,
     memset(&ty, 0, sizeof(ty));
     const int esize = y_f16 ? 2 : 4;
     const int y_tma = make_rowmajor_map(&ty, Y, esize, M, N, ldy, BW, 32) ? 1 : 0;
-    Params p{M, N, K, Y, ldy, y_f16, y_tma, prefetch, units, ws, flags, ds->d_error};
+    Params p{M, N, K, Y, ldy, y_f16, y_tma, prefetch, units, ws, flags, ds->d_error, (const uint8_t *)W, row_bytes};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(NT);
@@ -858,11 +965,11 @@ static size_t ws_bytes_q(int M, int N, int K) {
 
 // Fused-dequant prefill GEMM; VKF_ERR_UNSUPPORTED when the format or the
 // buffer geometry is not one it serves (the caller then widens W first):
-// Q4_0, Q8_0, Q4_K, Q5_K with K a multiple of 256, W 16-byte aligned; X fp16
+// Q4_0, Q8_0, Q4_K, Q5_K, Q6_K with K a multiple of 256, W 16-byte aligned; X fp16
 // rows 16-byte aligned.
 bool qgemm_supported(int wtype, const void *W, int K) {
     return (wtype == VKF_DEQUANT_Q4_0 || wtype == VKF_DEQUANT_Q8_0 || wtype == VKF_DEQUANT_Q4_K ||
-            wtype == VKF_DEQUANT_Q5_K) &&
+            wtype == VKF_DEQUANT_Q5_K || wtype == VKF_DEQUANT_Q6_K) &&
            K % qgemm::RV == 0 && ((uintptr_t)W & 15) == 0;
 }
 
@@ -873,6 +980,7 @@ size_t qgemm_ws_bytes(int wtype, int M, int N, int K) {
     case VKF_DEQUANT_Q8_0: return qgemm::ws_bytes_q<VKF_DEQUANT_Q8_0>(M, N, K);
     case VKF_DEQUANT_Q4_K: return qgemm::ws_bytes_q<VKF_DEQUANT_Q4_K>(M, N, K);
     case VKF_DEQUANT_Q5_K: return qgemm::ws_bytes_q<VKF_DEQUANT_Q5_K>(M, N, K);
+    case VKF_DEQUANT_Q6_K: return qgemm::ws_bytes_q<VKF_DEQUANT_Q6_K>(M, N, K);
     default: return 0;
     }
 }
@@ -889,6 +997,7 @@ int qgemm_launch(int wtype, const void *W, const void *X, int64_t ldx, void *Y, 
     case VKF_DEQUANT_Q8_0: return qgemm::launch_q<VKF_DEQUANT_Q8_0>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
     case VKF_DEQUANT_Q4_K: return qgemm::launch_q<VKF_DEQUANT_Q4_K>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
     case VKF_DEQUANT_Q5_K: return qgemm::launch_q<VKF_DEQUANT_Q5_K>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
+    case VKF_DEQUANT_Q6_K: return qgemm::launch_q<VKF_DEQUANT_Q6_K>(W, X, ldx, Y, y_f16, ldy, M, N, K, ws, prefetch, stream);
     default: return VKF_ERR_UNSUPPORTED;
     }
 }
