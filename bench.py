@@ -209,10 +209,11 @@ def stack_groups():
             ("down", S.Q6_K, FFN, HIDDEN, "f")]
 
 
-def stack_links():
+def stack_links(layers=None):
     """The stack's linears in order: (name, qtype, K, N, input), the output
-    head last."""
-    return [g for _ in range(LAYERS) for g in stack_groups()] + [("head", S.Q6_K, HIDDEN, VOCAB, "h")]
+    head last.  layers: fewer than the model's 48 only for profiler captures."""
+    n = LAYERS if layers is None else layers
+    return [g for _ in range(n) for g in stack_groups()] + [("head", S.Q6_K, HIDDEN, VOCAB, "h")]
 
 
 def link_seed(rank: int, i: int) -> int:
@@ -234,19 +235,24 @@ class Stack:
     vkflame_quant_linear_gather launch per linear (N = 1: independent
     vkflame_quant_linear_ex launches), for comparison."""
 
-    def __init__(self, world, rank, dist, stream, mode="chained", trace=False):
+    def __init__(self, world, rank, dist, stream, mode="chained", trace=False, layers=None):
         import torch
         from vkflame_b200 import rt, shard
         from vkflame_b200.gather import GatherGroup
         self.rt, self.world, self.rank, self.dist, self.stream, self.mode = rt, world, rank, dist, stream, mode
-        self.x_h = torch.randn((1, HIDDEN), device="cuda").half()
+        # Chained forms: a small input row (N(0,1) x 1e-3) so that the first
+        # layer's outputs stay finite in fp16 (with these random weights each
+        # link multiplies the magnitudes by ~100) and can be checked; the
+        # deeper layers' values overflow, which changes no timing.
+        scale = 1.0 if mode == "independent" else 1e-3
+        self.x_h = (torch.randn((1, HIDDEN), device="cuda") * scale).half()
         self.x_f = torch.randn((1, FFN), device="cuda").half()
         self.weight_bytes = 0
         self.gg = GatherGroup(dist, world, rank)
         self.links = []   # (name, q, K, n, weight, out buffer or plain tensor, x source index or -1)
         self.ops = []     # "launches" mode: (q, K, n, w, x tensor, out, vkf_gather_t)
         chain = []
-        for i, (name, q, K, N, inp) in enumerate(stack_links()):
+        for i, (name, q, K, N, inp) in enumerate(stack_links(layers)):
             r0, r1 = shard.row_range(N, world, rank)  # this rank's output rows (vkflame_b200/shard.py)
             n = r1 - r0
             w = make_quant_weight_gpu(q, n, K, link_seed(rank, i))
@@ -302,14 +308,17 @@ class Stack:
         self.gg.close()
 
     # ---------------------------------------------------------- parity ----
-    def parity(self, sample=("o", "down", "head")):
+    def parity(self, sample=(0, 1, 2, 3)):
         """Checks of the last run's outputs, outside the timed region.
         ranks_identical: every rank holds the same gathered words (a
         position-weighted checksum per buffer, all-gathered).  vs_unsharded:
-        on rank 0, the full (unsharded) weights of sampled links regenerated
-        from every rank's seeds, run through the single-GPU decode GEMV
-        (vkflame_quant_linear_ex) on the same gathered input, against the
-        gathered output; normwise max |y - r| / max |r|."""
+        on rank 0, the full (unsharded) weights of the first layer's links
+        (qk and v read the token's row, o reads qk's gathered output, gate_up
+        o's; Q4_K and Q6_K) regenerated from every rank's seeds, run through
+        the single-GPU decode GEMV (vkflame_quant_linear_ex) on the same
+        gathered input, against the gathered output; normwise
+        max |y - r| / max |r|.  Deeper layers' values overflow fp16 (random
+        weights), so they are covered by ranks_identical only."""
         import torch
         from vkflame_b200 import shard
         if self.mode == "independent":
@@ -333,9 +342,7 @@ class Stack:
         if self.rank != 0:
             return out
         errs = {}
-        names = [lk[0] for lk in self.links]
-        picks = [names.index(sample[0]), len(names) - 1 - names[::-1].index(sample[1]), names.index(sample[2])]
-        for i in picks:
+        for i in sample:
             name, q, K, n, w, y, src = self.links[i]
             N = n * self.world
             wfull = torch.cat([make_quant_weight_gpu(q, shard.row_range(N, self.world, r)[1] -
@@ -376,7 +383,7 @@ def run_stack(args, world, rank, local, dist, mode, steps, e2e=True, trace=False
     s = torch.cuda.Stream()
     res = {}
     with torch.cuda.stream(s):
-        st = Stack(world, rank, dist, s.cuda_stream, mode=mode, trace=trace)
+        st = Stack(world, rank, dist, s.cuda_stream, mode=mode, trace=trace, layers=args.layers)
         st.step()  # one-time setup outside the capture
         torch.cuda.synchronize()
         l0 = rt.launch_count()
@@ -446,8 +453,9 @@ def bench_stack(args, world, rank, local, dist):
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "q4_K/q6_K weights x f16 activations, f32 accumulation",
         "data": "synthetic: seeded random ggml blocks (fp16 scales U[1e-3,1e-2]), N(0,1) fp16 activations",
-        "config": {"workload": "config 5: Qwen2-14B linear stack, 48 layers + output head, M=1 decode",
-                   "layers": LAYERS, "hidden": HIDDEN, "ffn": FFN, "vocab": VOCAB,
+        "config": {"workload": "config 5: Qwen2-14B linear stack, 48 layers + output head, M=1 decode"
+                               if args.layers == LAYERS else f"profiling cut: {args.layers} layers + output head",
+                   "layers": args.layers, "hidden": HIDDEN, "ffn": FFN, "vocab": VOCAB,
                    "weight_gb_per_token": total_bytes / 1e9, "column_shards": world,
                    "kernel": ("one persistent kernel per token (vkflame_chain_run)" if args.stack_mode != "launches"
                               else "one decode GEMV launch per linear"),
@@ -745,6 +753,61 @@ def cpu_baseline_stack(budget_s=12.0):
                       f"of the stack ({el:.1f} s)"}
 
 
+def gemv_timeline(args, world, rank, dist):
+    """One token of the per-linear-launch stack with the diagnostic GEMV build:
+    for each launch the first CTA start and last CTA end, and per CTA the
+    start, dependency release, activations ready, decode loop end and reducer
+    end (globaltimer ns).  Prints a per-shape summary (medians over layers)."""
+    import ctypes as C
+    import torch
+    from vkflame_b200 import rt
+    lib = rt.lib()
+    if not hasattr(lib, "vkf_gemv_timeline"):
+        raise SystemExit("--gemv-timeline needs the diagnostic build (VKFLAME_RT_LIB=.../lib/timing/libvkflame_rt.so)")
+    lib.vkf_gemv_timeline.argtypes = [C.c_void_p, C.c_int]
+    lib.vkf_gemv_cta_times.argtypes = [C.c_void_p, C.c_int]
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        st = Stack(world, rank, dist, s.cuda_stream, mode="launches", layers=args.layers)
+        st.step()
+        torch.cuda.synchronize()
+        lib.vkf_gemv_timeline(None, 1)  # launch ids restart at 0 for the captured graph
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            st.step()
+        for _ in range(args.warmup):
+            g.replay()
+        barrier(dist)
+        lib.vkf_gemv_timeline(None, 1)
+        barrier(dist)
+        e0, e1 = timed_graph(g, s, 1)
+        torch.cuda.synchronize()
+    n = len(st.ops)
+    tl = np.zeros((4096, 3), np.uint64)
+    lib.vkf_gemv_timeline(tl.ctypes.data, 0)
+    cta = np.zeros((n, 512, 5), np.uint64)
+    for i in range(n):
+        lib.vkf_gemv_cta_times(cta[i].ctypes.data, i)
+    tl, cta = tl[:n].astype(np.int64), cta.astype(np.int64)
+    rows = {}
+    for i, (name, q, K, nn, *_) in enumerate(st.links):
+        c = cta[i][cta[i][:, 0] > 0]
+        prev_end = tl[i - 1][1] if i else tl[i][0]
+        rows.setdefault(name, []).append([(c[:, 0].max() - c[:, 0].min()) / 1e3, np.median(c[:, 1] - c[:, 0]) / 1e3,
+                                          np.median(c[:, 2] - c[:, 1]) / 1e3, np.median(c[:, 3] - c[:, 2]) / 1e3,
+                                          np.median(c[:, 4] - c[:, 3]) / 1e3, (tl[i][1] - tl[i][0]) / 1e3,
+                                          (tl[i][1] - prev_end) / 1e3, len(c)])
+    if rank == 0:
+        print(f"token {e0.elapsed_time(e1):.3f} ms (diagnostic build), {n} launches, world {world}")
+        print("linear | CTAs | CTA start spread | start->dep release | dep->X ready | decode loop | "
+              "reducer tail | launch span | end - previous end  (us, medians over layers)")
+        for name, r in rows.items():
+            m = np.median(np.array(r), axis=0)
+            print(f"{name} | {int(m[7])} | {m[0]:.2f} | {m[1]:.2f} | {m[2]:.2f} | {m[3]:.2f} | {m[4]:.2f} | "
+                  f"{m[5]:.2f} | {m[6]:.2f}")
+    st.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -756,7 +819,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 1-4 sub-benchmarks")
     ap.add_argument("--stack-mode", default="chained", choices=["chained", "independent", "launches"])
+    ap.add_argument("--layers", type=int, default=LAYERS, help="fewer layers only for profiler captures")
     ap.add_argument("--trace", action="store_true", help="record per-linear chain timestamps (gpurun_out/)")
+    ap.add_argument("--gemv-timeline", action="store_true",
+                    help="with --stack-mode launches and the diagnostic build (make -C vkflame_b200/csrc timing; "
+                         "VKFLAME_RT_LIB=vkflame_b200/lib/timing/libvkflame_rt.so): per-launch and per-CTA "
+                         "timestamps of one token, summarised on stdout")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_env()
@@ -783,6 +851,11 @@ def main():
         return
 
     dist = init_dist(world, local)
+    if args.gemv_timeline:
+        gemv_timeline(args, world, rank, dist)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
     line = bench_stack(args, world, rank, local, dist)
     if rank == 0 and world == 1:
         if not args.no_extras:

@@ -191,6 +191,11 @@ int vkflame_chain_epoch(const vkf_chain_t *chain, int *epoch);
 /* VKF_CHAIN_TRACE: per linear {latest time a CTA had its X ready, latest
  * output store} of the last run, globaltimer ns (host array of 2n). */
 int vkflame_chain_trace(const vkf_chain_t *chain, unsigned long long *times);
+/* First wait that gave up inside the chain kernel since creation (all zero:
+ * none): {role (1 weight producer, 2 reducer, 3 consumer waiting for
+ * weights, 4 consumer waiting for a partial slot, 5 activations), linear
+ * index, item (or row block / run), CTA}.  Each wait gives up after 2 s. */
+int vkflame_chain_status(const vkf_chain_t *chain, int *fail4);
 int vkflame_chain_destroy(vkf_chain_t *chain);
 
 /* CUDA IPC for the gathered buffers and counters: a 64-byte handle of the

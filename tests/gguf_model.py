@@ -10,7 +10,10 @@ from vkflame_b200 import gguf
 from vkflame_b200 import synth as S
 
 
-def make(path, layers=2, hidden=512, heads=4, kv_heads=2, head_dim=128, ffn=1280, vocab=2048, seed=0):
+def make(path, layers=2, hidden=512, heads=4, kv_heads=2, head_dim=128, ffn=1280, vocab=2048, seed=0, d_range=None):
+    """d_range: the fp16 block scales' range (default: the synthetic
+    generator's U[1e-3, 1e-2]; the GPU test picks small ones so that a chain
+    of linears stays finite in fp16)."""
     meta = {"general.architecture": "qwen2", "general.name": "synthetic-test", "qwen2.block_count": layers,
             "qwen2.embedding_length": hidden, "qwen2.feed_forward_length": ffn,
             "qwen2.attention.head_count": heads, "qwen2.attention.head_count_kv": kv_heads,
@@ -22,7 +25,7 @@ def make(path, layers=2, hidden=512, heads=4, kv_heads=2, head_dim=128, ffn=1280
     def q(name, fmt, K, N):
         nonlocal s
         s += 1
-        tensors.append((name, (K, N), gguf.VKF_TO_GGML[fmt], S.quant_matrix(fmt, N, K, seed=s)))
+        tensors.append((name, (K, N), gguf.VKF_TO_GGML[fmt], S.quant_matrix(fmt, N, K, seed=s, d_range=d_range)))
 
     rng = np.random.default_rng(seed)
     tensors.append(("token_embd.weight", (hidden, vocab), gguf.GGML_F16,

@@ -35,6 +35,12 @@ LINKS = [(S.Q4_K, 1024, 768, -1),   # 0: reads the input (K 1024)
 RUNS = 3
 
 
+def _drange(q):
+    """Block scales small enough that the chain's values stay finite in fp16
+    (with the benchmark's U[1e-3, 1e-2] each link grows them ~100x)."""
+    return (2e-5, 1e-4)
+
+
 @pytest.fixture(scope="module")
 def rt():
     from vkflame_b200 import rt as _rt
@@ -43,7 +49,7 @@ def rt():
 
 
 def _weights():
-    return [S.quant_matrix(q, N, K, seed=40 + i) for i, (q, K, N, _) in enumerate(LINKS)]
+    return [S.quant_matrix(q, N, K, seed=40 + i, d_range=_drange(q)) for i, (q, K, N, _) in enumerate(LINKS)]
 
 
 def _dq(q, w, N, K):
@@ -66,10 +72,12 @@ def test_chain_world1_matches_fp64_and_gemv(rt):
         for run in range(1, RUNS + 1):
             ch.run(0)
             torch.cuda.synchronize()
+            assert ch.status() == [0, 0, 0, 0], ch.status()
             rt.check_kernel_errors()
             assert ch.epoch() == run
             ys = [unpack(o.tensor.cpu().numpy(), run) for o in outs]
             for i, (q, K, N, src) in enumerate(LINKS):
+                assert np.isfinite(ys[i]).all(), (run, i)
                 xin = x if src < 0 else ys[src][:, :K]
                 ref = xin.astype(np.float64) @ _dq(q, ws[i], N, K).T
                 got = ys[i].astype(np.float64)
@@ -153,6 +161,7 @@ def _worker(rank, world, port, outdir):
     for _ in range(RUNS):
         ch.run(s.cuda_stream)
     torch.cuda.synchronize()
+    assert ch.status() == [0, 0, 0, 0], ch.status()
     rt.check_kernel_errors()
     assert ch.epoch() == RUNS
     for i, o in enumerate(outs):

@@ -18,13 +18,16 @@ def test_gguf_stack_two_steps(tmp_path):
     from vkflame_b200.stack import GGUFStack
     rt.lib()
     p = tmp_path / "m.gguf"
-    gguf_model.make(p, layers=2)
+    gguf_model.make(p, layers=2, d_range=(1e-5, 5e-5))  # values stay finite through 11 chained links
     st = GGUFStack(p)
     try:
         hidden = st.x.shape[1]
         for step in range(2):
             x = np.random.default_rng(step).standard_normal(hidden).astype(np.float16)
             st.step(x)
+            import torch
+            torch.cuda.synchronize()
+            assert st.chain.status() == [0, 0, 0, 0], st.chain.status()
             rt.check_kernel_errors()
             outs = {name: st.output(name) for name, *_ in st.links}
             for name, kind, K, N, tensors, src in st.links:
@@ -32,6 +35,7 @@ def test_gguf_stack_two_steps(tmp_path):
                 w = np.concatenate([po.dequant(kind, st.file.weight(t)[3], st.file.weight(t)[2] * K // 256)
                                     .reshape(-1, K) for t in tensors])
                 ref = xin.astype(np.float64) @ w.astype(np.float64).T
+                assert np.isfinite(outs[name]).all(), (step, name)
                 assert G.normwise_err(outs[name].astype(np.float64), ref) < G.REL_TOL, (step, name)
         assert outs["head"].shape == (1, 2048)
     finally:

@@ -30,7 +30,8 @@
 // (include/vkflame_rt.h): an aligned 8-byte store is single-copy atomic, so
 // a reader that sees its epoch in a word sees the values; two buffers by the
 // run's parity; the run count (epoch) is advanced by the grid's last CTA.
-// Every wait is bounded (error bit, then the kernel walks on without waiting).
+// Every wait is bounded in time (error bit and the place it gave up, then the
+// kernel walks on without waiting).
 //
 // Replaces, for a whole decode step, the per-call chain of the reference's
 // quantised mul_mat (shim/hip_runtime_shim.cpp:1102-1172): one launch per
@@ -85,6 +86,8 @@ struct Params {
     int *epoch, *done;
     unsigned *err;
     unsigned long long *trace;  // optional [n][2]: latest X-ready, latest row-block store over CTAs (globaltimer ns)
+    int *fail;                  // [4]: first wait that gave up: role (1 producer, 2 reducer, 3 consumer
+                                // ring, 4 consumer park slot, 5 activations), linear, item, CTA
 };
 
 __device__ __forceinline__ int first_item(int c, int I, int G) { return (int)((int64_t)c * I / G); }
@@ -94,6 +97,40 @@ __device__ __forceinline__ unsigned long long gtimer() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
+}
+
+// Every wait gives up after WAIT_NS of globaltimer time (or at once, after a
+// short grace, when another wait on this device already gave up), sets the
+// kernel error bit and records the first failure's place; the kernel then
+// walks on without waiting, so it always ends.
+constexpr unsigned long long WAIT_NS = 2000000000ull;
+
+__device__ __forceinline__ bool gave_up(unsigned *err) {
+    return (*(volatile unsigned *)err & VKF_KERR_WAIT_TIMEOUT) != 0;
+}
+
+__device__ __noinline__ void record_fail(const Params &p, int role, int li, int it) {
+    atomicOr(p.err, VKF_KERR_WAIT_TIMEOUT);
+    if (atomicCAS(&p.fail[0], 0, role) == 0) {
+        p.fail[1] = li;
+        p.fail[2] = it;
+        p.fail[3] = blockIdx.x;
+    }
+}
+
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, const Params &p, int role, int li, int it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = gtimer();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63) == 0) {
+            const unsigned long long dt = gtimer() - t0;
+            if (dt > WAIT_NS || (dt > 1000000ull && gave_up(p.err))) {
+                record_fail(p, role, li, it);
+                return false;
+            }
+        }
+    }
 }
 
 // Byte ring placement: deterministic in the item sequence, so the producer
@@ -106,7 +143,7 @@ __device__ __forceinline__ int ring_place(int &head, int bytes, int ring) {
 
 // 32 fp16 activations (run sb) of a plain row or of a gathered buffer (16
 // words {half2, epoch}; re-read until every word carries ep, bounded).
-__device__ __forceinline__ void load_run(const Lin &L, int ep, int sb, uint4 (&v)[4], unsigned *err) {
+__device__ __forceinline__ void load_run(const Lin &L, int ep, int sb, uint4 (&v)[4], const Params &p, int li) {
     if (!L.x_ll) {
         const uint4 *src = reinterpret_cast<const uint4 *>(L.X + sb * 64);
 #pragma unroll
@@ -115,6 +152,7 @@ __device__ __forceinline__ void load_run(const Lin &L, int ep, int sb, uint4 (&v
     }
     const uint8_t *src = L.X + (int64_t)(ep & 1) * L.x_stride + sb * 128;
     uint32_t d[16];
+    unsigned long long t0 = 0;
     for (uint32_t n = 0;; ++n) {
         uint32_t e[16];
 #pragma unroll
@@ -127,12 +165,13 @@ __device__ __forceinline__ void load_run(const Lin &L, int ep, int sb, uint4 (&v
 #pragma unroll
         for (int i = 0; i < 16; ++i) all = all && e[i] == (uint32_t)ep;
         if (all) break;
-        // Bounded: give up after 2^22 polls, or at once (after a short grace)
-        // once any wait of this device has given up, so a broken chain
-        // ends quickly instead of timing out link by link.
-        if (n == (1u << 22) || ((n & 1023u) == 1023u && (*(volatile unsigned *)err & VKF_KERR_WAIT_TIMEOUT))) {
-            atomicOr(err, VKF_KERR_WAIT_TIMEOUT);
-            break;
+        if (n == 0) t0 = gtimer();
+        else if ((n & 15) == 0) {
+            const unsigned long long dt = gtimer() - t0;
+            if (dt > WAIT_NS || (dt > 1000000ull && gave_up(p.err))) {
+                record_fail(p, 5, li, sb);
+                break;
+            }
         }
         __nanosleep(32);
     }
@@ -265,7 +304,7 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
                         clash = off < q_off[s] + q_len[s] && q_off[s] < off + bytes;
                     }
                     if (!clash) break;
-                    if (!mbar_wait(&empty[oldest % NSLOT], (uint32_t)(oldest / NSLOT) & 1u, p.err)) {
+                    if (!wait_bar(&empty[oldest % NSLOT], (uint32_t)(oldest / NSLOT) & 1u, p, 1, li, it)) {
                         ok = false;
                         break;
                     }
@@ -320,7 +359,7 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
             const int first_tile = i0 / L.S, last_tile = (i1 - 1) / L.S;
             for (int tb = first_tile; tb <= last_tile; ++tb, ++k) {
                 const int sl = k % PSLOTS;
-                if (ok) ok = mbar_wait(&parked[sl], (uint32_t)(k / PSLOTS) & 1u, p.err);
+                if (ok) ok = wait_bar(&parked[sl], (uint32_t)(k / PSLOTS) & 1u, p, 2, li, tb);
                 const float *q = park + (size_t)sl * CW * 32 * 2;
                 // lane = (row r = lane & 15, warp half h = lane >> 4): rows g < 8
                 // are .x of lanes g*4 + t, rows g + 8 are .y.
@@ -405,7 +444,7 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
         consumer_bar();
         for (int sb = r0 + threadIdx.x; sb < r1; sb += CW * 32) {
             uint4 v[4];
-            load_run(L, ep, sb, v, p.err);
+            load_run(L, ep, sb, v, p, li);
             quantize_run(v, sb, q6, xs, sums);
         }
         consumer_bar();
@@ -414,7 +453,7 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
         for (int it = i0; it < i1; ++it, ++n) {
             const int s = n % NSLOT;
             const int off = ring_place(head, L.item_bytes, p.ring_bytes);
-            if (ok) ok = mbar_wait(&full[s], (uint32_t)(n / NSLOT) & 1u, p.err);
+            if (ok) ok = wait_bar(&full[s], (uint32_t)(n / NSLOT) & 1u, p, 3, li, it);
             const int tile = it / L.S, step = it - tile * L.S;
             const int u0 = step * L.upi, nu = min(L.upi, L.units - u0);
             if (ok) {
@@ -460,7 +499,7 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
             const bool tile_end = step == L.S - 1 || it + 1 == i1;
             if (!tile_end) continue;
             const int sl = park_slot;
-            if (k >= PSLOTS && ok) ok = mbar_wait(&freed[sl], park_phase ^ 1u, p.err);
+            if (k >= PSLOTS && ok) ok = wait_bar(&freed[sl], park_phase ^ 1u, p, 4, li, it);
             float *pp = park + ((size_t)(sl * CW + warp) * 32 + lane) * 2;
             *reinterpret_cast<float2 *>(pp) = make_float2(acc[0] + acc[1], acc[2] + acc[3]);
             acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
@@ -651,6 +690,7 @@ extern "C" int vkflame_chain_create(const vkf_chain_linear_t *lin, int n, int wo
     p.off_bar = p.off_ring + ring;
     p.epoch = (int *)(base + off_ctl);
     p.done = (int *)(base + off_ctl + 4);
+    p.fail = (int *)(base + off_ctl + 16);
     p.err = ds->d_error;
     p.trace = tracing ? (unsigned long long *)(base + off_trace) : nullptr;
     c->trace = p.trace;
@@ -704,6 +744,13 @@ extern "C" int vkflame_chain_epoch(const vkf_chain_t *c, int *host) {
     if (!c || !host) return set_status(VKF_ERR_INVALID);
     return set_status(cudaMemcpy(host, c->p.epoch, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess ? VKF_OK
                                                                                                        : VKF_ERR_CUDA);
+}
+
+extern "C" int vkflame_chain_status(const vkf_chain_t *c, int *fail) {
+    if (!c || !fail) return set_status(VKF_ERR_INVALID);
+    return set_status(cudaMemcpy(fail, c->p.fail, 4 * sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess
+                          ? VKF_OK
+                          : VKF_ERR_CUDA);
 }
 
 extern "C" int vkflame_chain_destroy(vkf_chain_t *c) {

@@ -57,6 +57,7 @@ _SIGS = {
     "vkflame_chain_run": ([C.c_void_p, C.c_void_p], C.c_int),
     "vkflame_chain_epoch": ([C.c_void_p, C.POINTER(C.c_int)], C.c_int),
     "vkflame_chain_trace": ([C.c_void_p, C.c_void_p], C.c_int),
+    "vkflame_chain_status": ([C.c_void_p, C.c_void_p], C.c_int),
     "vkflame_chain_destroy": ([C.c_void_p], C.c_int),
     "vkflame_set_stream": ([C.c_void_p], C.c_int),
     "vkflame_dispatch_elementwise_f32": ([C.c_void_p] * 3 + [C.c_uint32] * 2, C.c_int),
@@ -202,6 +203,13 @@ class Chain:
         t = np.zeros((self.n, 2), np.uint64)
         _check(lib().vkflame_chain_trace(self.handle, t.ctypes.data), "chain_trace")
         return t
+
+    def status(self) -> list:
+        """First wait that gave up: [role, linear, item, CTA] (zeros: none)."""
+        import numpy as np
+        f = np.zeros(4, np.int32)
+        _check(lib().vkflame_chain_status(self.handle, f.ctypes.data), "chain_status")
+        return [int(v) for v in f]
 
     def close(self) -> None:
         if self.handle:
