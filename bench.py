@@ -240,11 +240,11 @@ class Stack:
         from vkflame_b200 import rt, shard
         from vkflame_b200.gather import GatherGroup
         self.rt, self.world, self.rank, self.dist, self.stream, self.mode = rt, world, rank, dist, stream, mode
-        # Chained forms: a small input row (N(0,1) x 1e-3) so that the first
+        # Chained forms: a small input row (N(0,1) x 1e-6) so that the first
         # layer's outputs stay finite in fp16 (with these random weights each
         # link multiplies the magnitudes by ~100) and can be checked; the
         # deeper layers' values overflow, which changes no timing.
-        scale = 1.0 if mode == "independent" else 1e-3
+        scale = 1.0 if mode == "independent" else 1e-6
         self.x_h = (torch.randn((1, HIDDEN), device="cuda") * scale).half()
         self.x_f = torch.randn((1, FFN), device="cuda").half()
         self.weight_bytes = 0
@@ -359,9 +359,12 @@ class Stack:
             errs[f"{name}#{i}"] = float((got - r).abs().max() / r.abs().max().clamp_min(1e-30))
             del wfull
         tol = 1e-3
-        out["vs_unsharded"] = {"links": errs, "max_normwise_err": max(errs.values()), "tol": tol,
+        finite = {k: v for k, v in errs.items() if np.isfinite(v)}
+        worst = max(finite.values()) if finite else float("nan")
+        out["vs_unsharded"] = {"links": errs, "max_normwise_err": worst, "tol": tol,
+                               "nonfinite": sorted(k for k in errs if k not in finite),
                                "reference": "vkflame_quant_linear_ex on the full weights (one GPU)",
-                               "pass": max(errs.values()) < tol}
+                               "pass": bool(finite) and len(finite) == len(errs) and worst < tol}
         return out
 
 

@@ -76,6 +76,15 @@ struct Lin {
     int *cnt;              // [T] arrival counters (zero between runs)
 };
 
+struct Geo {
+    const uint8_t *W;
+    int64_t row_bytes;
+    int qt, units, ub, S, upi, I, N, whole, rpb, item_bytes;
+};
+__device__ __forceinline__ Geo geo(const Lin &L) {
+    return Geo{L.W, L.row_bytes, L.qt, L.units, L.ub, L.S, L.upi, L.I, L.N, L.whole, L.rpb, L.item_bytes};
+}
+
 struct Params {
     const Lin *lin;
     int n;
@@ -291,9 +300,12 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
         bool ok = true;
         for (int li = 0; li < p.n && ok; ++li) {
             const Lin &L = p.lin[li];
-            const int i0 = first_item(cta, L.I, G), i1 = first_item(cta + 1, L.I, G);
+            // The hot fields in registers (every asm "memory" clobber would
+            // otherwise force a reload from global memory).
+            const Geo H = geo(L);
+            const int i0 = first_item(cta, H.I, G), i1 = first_item(cta + 1, H.I, G);
             for (int it = i0; it < i1; ++it, ++n) {
-                const int bytes = L.item_bytes;
+                const int bytes = H.item_bytes;
                 const int off = ring_place(head, bytes, p.ring_bytes);
                 // Wait until the oldest items in flight no longer overlap
                 // [off, off + bytes) and a slot is free.
@@ -314,23 +326,23 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
                 const int s = n % NSLOT;
                 q_off[s] = off;
                 q_len[s] = bytes;
-                const int tile = it / L.S, step = it - tile * L.S;
+                const int tile = it / H.S, step = it - tile * H.S;
                 uint8_t *dst = ring + off;
-                if (L.whole) {
+                if (H.whole) {
                     if (lane == 0) {
-                        const int rows = min(16, L.N - tile * 16);
-                        const uint32_t sz = (uint32_t)(((int64_t)rows * L.row_bytes + 15) & ~(int64_t)15);
+                        const int rows = min(16, H.N - tile * 16);
+                        const uint32_t sz = (uint32_t)(((int64_t)rows * H.row_bytes + 15) & ~(int64_t)15);
                         mbar_arrive_expect_tx(&full[s], sz);
-                        bulk_g2s(dst, L.W + (int64_t)tile * 16 * L.row_bytes, sz, &full[s]);
+                        bulk_g2s(dst, H.W + (int64_t)tile * 16 * H.row_bytes, sz, &full[s]);
                     }
                 } else {
-                    const int u0 = step * L.upi, nu = min(L.upi, L.units - u0);
-                    const int64_t b0 = (int64_t)u0 * L.ub, b1 = (int64_t)(u0 + nu) * L.ub;
+                    const int u0 = step * H.upi, nu = min(H.upi, H.units - u0);
+                    const int64_t b0 = (int64_t)u0 * H.ub, b1 = (int64_t)(u0 + nu) * H.ub;
                     const int row = tile * 16 + lane;
                     uint32_t sz = 0;
                     const uint8_t *src = nullptr;
-                    if (lane < 16 && row < L.N) {
-                        const uint8_t *q = L.W + (int64_t)row * L.row_bytes + b0;
+                    if (lane < 16 && row < H.N) {
+                        const uint8_t *q = H.W + (int64_t)row * H.row_bytes + b0;
                         const uint32_t mis = (uint32_t)((uintptr_t)q & 15);
                         src = q - mis;
                         sz = (uint32_t)((mis + (b1 - b0) + 15) & ~15);
@@ -340,7 +352,7 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
                     for (int o = 8; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
                     if (lane == 0) mbar_arrive_expect_tx(&full[s], total);
                     __syncwarp();
-                    if (sz) bulk_g2s(dst + lane * L.rpb, src, sz, &full[s]);
+                    if (sz) bulk_g2s(dst + lane * H.rpb, src, sz, &full[s]);
                 }
                 __syncwarp();
             }
@@ -354,9 +366,12 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
         bool ok = true;
         for (int li = 0; li < p.n; ++li) {
             const Lin &L = p.lin[li];
-            const int i0 = first_item(cta, L.I, G), i1 = first_item(cta + 1, L.I, G);
+            // The hot fields in registers (every asm "memory" clobber would
+            // otherwise force a reload from global memory).
+            const Geo H = geo(L);
+            const int i0 = first_item(cta, H.I, G), i1 = first_item(cta + 1, H.I, G);
             if (i1 <= i0) continue;
-            const int first_tile = i0 / L.S, last_tile = (i1 - 1) / L.S;
+            const int first_tile = i0 / H.S, last_tile = (i1 - 1) / H.S;
             for (int tb = first_tile; tb <= last_tile; ++tb, ++k) {
                 const int sl = k % PSLOTS;
                 if (ok) ok = wait_bar(&parked[sl], (uint32_t)(k / PSLOTS) & 1u, p, 2, li, tb);
@@ -372,8 +387,8 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
                 v += __shfl_xor_sync(0xffffffffu, v, 16);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&freed[sl]);
-                const bool valid = lane < 16 && tb * 16 + lane < L.N;
-                const bool whole = tb * L.S >= i0 && (tb + 1) * L.S <= i1;
+                const bool valid = lane < 16 && tb * 16 + lane < H.N;
+                const bool whole = tb * H.S >= i0 && (tb + 1) * H.S <= i1;
                 if (whole) {
                     store_block(L, p.nranks, ep, tb * 16, v, valid);
                 } else {
@@ -384,8 +399,8 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
                     // The tile's contributors are the owners of its S items (with
                     // fewer items than CTAs, CTAs between them may own none).
                     int owners = 0;
-                    for (int i = tb * L.S, prev = -1; i < (tb + 1) * L.S; ++i) {
-                        const int c = cta_of_item(i, L.I, G);
+                    for (int i = tb * H.S, prev = -1; i < (tb + 1) * H.S; ++i) {
+                        const int c = cta_of_item(i, H.I, G);
                         owners += c != prev;
                         prev = c;
                     }
@@ -399,11 +414,11 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
                     if (__shfl_sync(0xffffffffu, fin, 0)) {
                         float t = 0.f;
                         if (lane < 16)
-                            for (int i = tb * L.S, prev = -1; i < (tb + 1) * L.S; ++i) {
-                                const int c = cta_of_item(i, L.I, G);
+                            for (int i = tb * H.S, prev = -1; i < (tb + 1) * H.S; ++i) {
+                                const int c = cta_of_item(i, H.I, G);
                                 if (c == prev) continue;
                                 prev = c;
-                                const int wc = tb == first_item(c, L.I, G) / L.S ? 0 : 1;
+                                const int wc = tb == first_item(c, H.I, G) / H.S ? 0 : 1;
                                 t += __ldcg(L.ws + ((int64_t)c * 2 + wc) * 16 + lane);
                             }
                         store_block(L, p.nranks, ep, tb * 16, t, valid);
@@ -432,15 +447,18 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int li = 0; li < p.n; ++li) {
         const Lin &L = p.lin[li];
-        const int i0 = first_item(cta, L.I, G), i1 = first_item(cta + 1, L.I, G);
+            // The hot fields in registers (every asm "memory" clobber would
+            // otherwise force a reload from global memory).
+            const Geo H = geo(L);
+        const int i0 = first_item(cta, H.I, G), i1 = first_item(cta + 1, H.I, G);
         if (i1 <= i0) continue;
-        const bool q6 = L.qt == VKF_DEQUANT_Q6_K, q5 = L.qt == VKF_DEQUANT_Q5_K;
+        const bool q6 = H.qt == VKF_DEQUANT_Q6_K, q5 = H.qt == VKF_DEQUANT_Q5_K;
         const int sum_b = q6 ? 96 : 64;
         // Activations of this linear: the runs of the units this CTA's items
         // cover.  The barrier before keeps the previous linear's readers.
-        const int ua = (i0 % L.S) * L.upi, ue = L.S == 1 ? L.units : std::min(L.units, ((i1 - 1) % L.S + 1) * L.upi);
-        const bool all_units = (i1 - i0) >= L.S || i0 / L.S != (i1 - 1) / L.S;
-        const int r0 = all_units ? 0 : ua * 8, r1 = all_units ? L.units * 8 : ue * 8;
+        const int ua = (i0 % H.S) * H.upi, ue = H.S == 1 ? H.units : std::min(H.units, ((i1 - 1) % H.S + 1) * H.upi);
+        const bool all_units = (i1 - i0) >= H.S || i0 / H.S != (i1 - 1) / H.S;
+        const int r0 = all_units ? 0 : ua * 8, r1 = all_units ? H.units * 8 : ue * 8;
         consumer_bar();
         for (int sb = r0 + threadIdx.x; sb < r1; sb += CW * 32) {
             uint4 v[4];
@@ -449,24 +467,24 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
         }
         consumer_bar();
         if (p.trace && threadIdx.x == 0) atomicMax(&p.trace[2 * li], gtimer());
-        const int64_t row_off_a = (int64_t)g * L.row_bytes, row_off_b = (int64_t)(g + 8) * L.row_bytes;
+        const int64_t row_off_a = (int64_t)g * H.row_bytes, row_off_b = (int64_t)(g + 8) * H.row_bytes;
         for (int it = i0; it < i1; ++it, ++n) {
             const int s = n % NSLOT;
-            const int off = ring_place(head, L.item_bytes, p.ring_bytes);
+            const int off = ring_place(head, H.item_bytes, p.ring_bytes);
             if (ok) ok = wait_bar(&full[s], (uint32_t)(n / NSLOT) & 1u, p, 3, li, it);
-            const int tile = it / L.S, step = it - tile * L.S;
-            const int u0 = step * L.upi, nu = min(L.upi, L.units - u0);
+            const int tile = it / H.S, step = it - tile * H.S;
+            const int u0 = step * H.upi, nu = min(H.upi, H.units - u0);
             if (ok) {
                 const uint8_t *st = ring + off;
                 const uint8_t *ra, *rb;
-                if (L.whole) {
+                if (H.whole) {
                     ra = st + row_off_a;
                     rb = st + row_off_b;
                 } else {
-                    const uintptr_t ga = (uintptr_t)L.W + ((int64_t)tile * 16 + g) * L.row_bytes + (int64_t)u0 * L.ub;
-                    const uintptr_t gb = ga + 8 * L.row_bytes;
-                    ra = st + g * L.rpb + (ga & 15);
-                    rb = st + (g + 8) * L.rpb + (gb & 15);
+                    const uintptr_t ga = (uintptr_t)H.W + ((int64_t)tile * 16 + g) * H.row_bytes + (int64_t)u0 * H.ub;
+                    const uintptr_t gb = ga + 8 * H.row_bytes;
+                    ra = st + g * H.rpb + (ga & 15);
+                    rb = st + (g + 8) * H.rpb + (gb & 15);
                 }
                 int u = warp - ubase;
                 if (u < 0) u += CW;
@@ -475,7 +493,7 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
                         const int unit = u0 + u;
                         const uint8_t *pa = ra + u * 210, *pb = rb + u * 210;
                         const float *sx = reinterpret_cast<const float *>(sums + unit * 96);
-                        if ((((uintptr_t)pa | (uintptr_t)pb) & 3) == 0) StepQ6i::run<true>(pa, pb, xs + unit * 512, g, sx, t, acc);
+                        if (__all_sync(0xffffffffu, (((uintptr_t)pa | (uintptr_t)pb) & 3) == 0)) StepQ6i::run<true>(pa, pb, xs + unit * 512, g, sx, t, acc);
                         else StepQ6i::run<false>(pa, pb, xs + unit * 512, g, sx, t, acc);
                     }
                 } else if (q5) {
@@ -496,7 +514,7 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
             while (ubase >= CW) ubase -= CW;
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
-            const bool tile_end = step == L.S - 1 || it + 1 == i1;
+            const bool tile_end = step == H.S - 1 || it + 1 == i1;
             if (!tile_end) continue;
             const int sl = park_slot;
             if (k >= PSLOTS && ok) ok = wait_bar(&freed[sl], park_phase ^ 1u, p, 4, li, it);

@@ -641,7 +641,7 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
                     const int unit = u0 + u;
                     const uint8_t *pa = ra + u * UB, *pb = rb + u * UB;
                     const float *sx = reinterpret_cast<const float *>(sums + unit * 96);
-                    if ((((uintptr_t)pa | (uintptr_t)pb) & 3) == 0) StepQ6i::run<true>(pa, pb, xs + unit * 512, g, sx, t, acc);
+                    if (__all_sync(0xffffffffu, (((uintptr_t)pa | (uintptr_t)pb) & 3) == 0)) StepQ6i::run<true>(pa, pb, xs + unit * 512, g, sx, t, acc);
                     else StepQ6i::run<false>(pa, pb, xs + unit * 512, g, sx, t, acc);
                 }
             } else {

@@ -444,12 +444,16 @@ template <bool Q5> struct StepK1i {
 // (x = s_j * (256 xh + xl) per 32-value run j = 4 ip + s); thread (g, t) owns
 // groups (ip, t, h) and adds  d * sc * (s_j * (256 Dh + Dl) - 32 * X16).
 // Odd super-blocks start 2 mod 4: their words are two aligned words and a
-// byte permute (AL4 = false).
+// funnel shift (AL4 = false, which serves any 2-byte alignment, so the choice
+// can be made warp-uniform: mma.sync must be executed by the whole warp).
 struct StepQ6i {
     template <bool AL4> __device__ __forceinline__ static uint32_t w32(const uint8_t *p) {
         if constexpr (AL4) return *reinterpret_cast<const uint32_t *>(p);
-        const uint32_t lo = *reinterpret_cast<const uint32_t *>(p - 2), hi = *reinterpret_cast<const uint32_t *>(p + 2);
-        return prmt(lo, hi, 0x5432);
+        // Any 2-byte aligned address (lanes of one warp may differ): the two
+        // aligned words around it, shifted by 0 or 16 bits.
+        const uintptr_t a = (uintptr_t)p;
+        const uint32_t *q = reinterpret_cast<const uint32_t *>(a & ~(uintptr_t)3);
+        return __funnelshift_r(q[0], q[1], (uint32_t)(a & 3) * 8);
     }
     template <int S> __device__ __forceinline__ static uint32_t code(uint32_t q0, uint32_t q1, uint32_t qh) {
         const uint32_t ql = (S & 1) ? q1 : q0;
