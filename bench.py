@@ -245,8 +245,10 @@ class Stack:
         # link multiplies the magnitudes by ~100) and can be checked; the
         # deeper layers' values overflow, which changes no timing.
         scale = 1.0 if mode == "independent" else 1e-6
-        self.x_h = (torch.randn((1, HIDDEN), device="cuda") * scale).half()
-        self.x_f = torch.randn((1, FFN), device="cuda").half()
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(1234)  # the same token row on every rank
+        self.x_h = (torch.randn((1, HIDDEN), device="cuda", generator=gen) * scale).half()
+        self.x_f = torch.randn((1, FFN), device="cuda", generator=gen).half()
         self.weight_bytes = 0
         self.gg = GatherGroup(dist, world, rank)
         self.links = []   # (name, q, K, n, weight, out buffer or plain tensor, x source index or -1)

@@ -28,9 +28,13 @@ def f32dev(a):
 
 
 def close(got, ref, rtol=2e-6, atol=1e-6):
-    got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
-    ok = np.abs(got - ref) <= atol + rtol * np.abs(ref)
-    return bool(ok.all()), float(np.abs(got - ref).max())
+    got, ref = np.asarray(got, np.float64).ravel(), np.asarray(ref, np.float64).ravel()
+    fin = np.isfinite(ref)
+    if not np.array_equal(np.isfinite(got), fin) or not np.array_equal(got[~fin], ref[~fin]):
+        return False, float("nan")  # infinities and NaNs must match in place (log(0) = -inf)
+    d = np.abs(got[fin] - ref[fin])
+    ok = d <= atol + rtol * np.abs(ref[fin])
+    return bool(ok.all()), float(d.max()) if d.size else 0.0
 
 
 @pytest.mark.parametrize("op", range(15))

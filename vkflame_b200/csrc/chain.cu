@@ -40,6 +40,7 @@
 #include "gemv_q.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 #include <vector>
 
 namespace vkf {
@@ -52,9 +53,9 @@ using gemv::m1_sum_slot;
 constexpr int CW = 8;                  // consumer warps
 constexpr int NT = 32 * (CW + 2);      // + producer + reducer
 constexpr int NSLOT = 8;               // ring items in flight
-constexpr int PSLOTS = 10;             // parked row blocks in flight
+constexpr int PSLOTS = 6;              // parked row blocks in flight
 constexpr int SMEM = 227 * 1024;
-constexpr int ROW_BUDGET = 4400;       // max bytes of one row per item
+constexpr int ROW_BUDGET = 4400;       // max bytes of one row per item (default)
 constexpr int PARK_BYTES = CW * 32 * 2 * 4;
 
 struct Lin {
@@ -579,6 +580,13 @@ extern "C" int vkflame_chain_create(const vkf_chain_linear_t *lin, int n, int wo
     DeviceState *ds = device_state();
     if (!ds) return set_status(VKF_ERR_NO_DEVICE);
     const int G = ds->sm_count;
+    // Bytes of one row per ring item (whole rows up to this, else K-ranges);
+    // VKFLAME_CHAIN_ROW_BUDGET overrides it for measurements.
+    static const int row_budget = [] {
+        const char *e = getenv("VKFLAME_CHAIN_ROW_BUDGET");
+        const int v = e ? atoi(e) : 0;
+        return v >= 256 ? v : ROW_BUDGET;
+    }();
     std::vector<Lin> L(n);
     int units_max = 1;
     for (int i = 0; i < n; ++i) {
@@ -598,7 +606,7 @@ extern "C" int vkflame_chain_create(const vkf_chain_linear_t *lin, int n, int wo
         if (c.wtype == VKF_DEQUANT_Q6_K ? (wa & 1) : (wa & 3)) return set_status(VKF_ERR_BADPTR);
         const bool owned = c.wtype != VKF_DEQUANT_Q6_K;
         d.T = (c.N + 15) / 16;
-        if (16 * d.row_bytes <= 16 * ROW_BUDGET && (wa & 15) == 0 && (16 * d.row_bytes) % 16 == 0 &&
+        if (16 * d.row_bytes <= 16 * row_budget && (wa & 15) == 0 && (16 * d.row_bytes) % 16 == 0 &&
             pitch_conflicts(d.row_bytes, owned) <= 2) {
             d.whole = 1;
             d.S = 1;
@@ -607,7 +615,7 @@ extern "C" int vkflame_chain_create(const vkf_chain_linear_t *lin, int n, int wo
             d.item_bytes = (int)up((size_t)16 * d.row_bytes, 128);
         } else {
             d.whole = 0;
-            const int upi_max = std::max(1, ROW_BUDGET / d.ub);
+            const int upi_max = std::max(1, row_budget / d.ub);
             d.S = (d.units + upi_max - 1) / upi_max;
             d.upi = (d.units + d.S - 1) / d.S;
             const int ng = ((d.upi * d.ub + 15) / 16 + 1) | 1;  // odd granule count per row

@@ -70,7 +70,8 @@ __global__ void __launch_bounds__(NT) map_kernel(const float *__restrict__ src, 
                                                  unsigned op, int kind, float scale, float bias, int vec) {
     const uint64_t stride = (uint64_t)gridDim.x * NT;
     uint64_t i = (uint64_t)blockIdx.x * NT + threadIdx.x;
-    auto f = [&](float x) { return kind == 0 ? unary(x, op) : scale * x + bias; };
+    // scale * x + bias as two roundings, as the shader states it (no fused multiply-add)
+    auto f = [&](float x) { return kind == 0 ? unary(x, op) : __fadd_rn(__fmul_rn(scale, x), bias); };
     if (vec) {
         const uint64_t n4 = n / 4;
         for (uint64_t j = i; j < n4; j += stride) {

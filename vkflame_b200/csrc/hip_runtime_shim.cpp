@@ -553,12 +553,17 @@ hipError_t hipLaunchKernel(const void *func, vkf_dim3 gridDim, vkf_dim3 blockDim
         return from_vkf(vkflame_dispatch_binop_f32(nullptr, ptr(0), ptr(1), ptr(2), (uint32_t)n, (uint32_t)n, op));
     }
     if (has("soft_max") || has("softmax")) {
-        // (x, mask, dst, ncols, ...) or the older (x, dst, ncols, ...): told
-        // apart by args[2] read as an int, as the reference did; rows = grid.y
+        // (x, mask, dst, ncols, ...) or the older (x, dst, ncols, ...).  The
+        // reference told them apart by reading args[2] as an int (> 0: new),
+        // which misreads a device pointer whose low word looks negative; here
+        // args[2] is the destination when it points into a known allocation.
         const uint32_t rows = gridDim.y > 0 ? gridDim.y : 1;
-        int ncols = i32(2);
+        void *base = nullptr;
+        size_t size = 0;
+        const bool new_sig = vkflame_ptr_lookup(ptr(2), &base, &size) == VKF_OK || i32(2) > 0;
+        int ncols;
         void *dst;
-        if (ncols > 0) {
+        if (new_sig) {
             dst = ptr(2);
             ncols = i32(3);
         } else {
