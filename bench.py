@@ -254,7 +254,14 @@ class Stack:
         self.links = []   # (name, q, K, n, weight, out buffer or plain tensor, x source index or -1)
         self.ops = []     # "launches" mode: (q, K, n, w, x tensor, out, vkf_gather_t)
         chain = []
-        for i, (name, q, K, N, inp) in enumerate(stack_links(layers)):
+        links = stack_links(layers)
+        if mode == "independent":
+            # same input row and format next to each other: the kernel keeps
+            # a quantised row resident across consecutive links
+            order = {"qk": 0, "o": 1, "gate_up": 2, "v": 3, "down": 4, "head": 5}
+            links = [l for lay in range(len(links) // 5) for l in sorted(links[5 * lay:5 * lay + 5],
+                                                                            key=lambda t: order[t[0]])] + links[-1:]
+        for i, (name, q, K, N, inp) in enumerate(links):
             r0, r1 = shard.row_range(N, world, rank)  # this rank's output rows (vkflame_b200/shard.py)
             n = r1 - r0
             w = make_quant_weight_gpu(q, n, K, link_seed(rank, i))
@@ -439,12 +446,28 @@ def run_stack(args, world, rank, local, dist, mode, steps, e2e=True, trace=False
 
 
 def bench_stack(args, world, rank, local, dist):
-    res = run_stack(args, world, rank, local, dist, args.stack_mode, args.steps, trace=args.trace)
+    """The headline.  Default (--stack-mode auto): at N = 1 the stack's
+    weight-streaming figure, every linear reading its layer input, as one
+    persistent kernel per token; at N > 1 the tensor-parallel form, every
+    linear waiting for the previous linear's gathered output, one fused
+    GEMV + all-gather launch per linear (measured faster than the persistent
+    kernel in chained form).  At N = 1 the chained form is also measured,
+    both ways, and reported in config (the like-for-like N = 1 figure for
+    the N > 1 runs)."""
+    mode = args.stack_mode
+    if mode == "auto":
+        mode = "independent" if world == 1 else "launches"
+    args.stack_mode = mode
+    res = run_stack(args, world, rank, local, dist, mode, args.steps, trace=args.trace)
     extra = {}
-    if world == 1 and not args.no_extras and args.stack_mode == "chained":
-        ind = run_stack(args, world, rank, local, dist, "independent", args.steps, e2e=False)
-        extra["independent_ms_per_token"] = ind["ms"]
-        extra["independent_gb_s"] = ind["weight_bytes"] / (ind["ms"] * 1e-3) / 1e9
+    if world == 1 and not args.no_extras:
+        for alt in ("launches", "chained"):
+            if alt == mode:
+                continue
+            r = run_stack(args, world, rank, local, dist, alt, args.steps, e2e=False)
+            extra[f"{alt}_ms_per_token"] = r["ms"]
+            extra[f"{alt}_gb_s"] = r["weight_bytes"] / (r["ms"] * 1e-3) / 1e9
+            extra[f"{alt}_parity"] = r["parity"]
     ms, ems = res["ms"], res["e2e_ms"]
     weight_bytes = res["weight_bytes"]
     total_bytes = weight_bytes * world  # every rank streams its shard once per token
@@ -473,10 +496,15 @@ def bench_stack(args, world, rank, local, dist):
                    "l2": "weights (9.0 GB) exceed L2; no flush needed", **extra},
         "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks.get("hbm_gbs") else "fallback",
-                     "traffic": weight_bytes * CHAIN_TRAFFIC_RATIO,
-                     "note": "dominant kernel = the per-token chain kernel (the only launch of the timed graph): "
-                             "algorithmic weight bytes per launch (this rank's shard of the token) / launch time; "
-                             "traffic = DRAM bytes per launch scaled from an ncu capture of the same kernel"},
+                     "traffic": (weight_bytes * CHAIN_TRAFFIC_RATIO if args.stack_mode != "launches"
+                                 else weight_bytes / max(1, res["launches_per_step"]) * GEMV_TRAFFIC_RATIO),
+                     "note": ("dominant kernel = the per-token chain kernel (the only launch of the timed graph): "
+                              "algorithmic weight bytes per launch (this rank's shard of the token) / launch time; "
+                              "traffic = DRAM bytes per launch scaled from an ncu capture of the same kernel")
+                             if args.stack_mode != "launches" else
+                             ("dominant kernel = gemv_kernel (every launch of the timed graph): algorithmic weight "
+                              "bytes per launch / average launch time (graph time / launches); traffic = DRAM bytes "
+                              "per launch from ncu captures of the kernel on the stack's shapes")},
         "e2e": {"value": total_bytes / (ems * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": HIDDEN * 2,
                 "d2h_bytes_per_step": res["d2h"], "ms_per_step": ems},
         "parity": res["parity"],
@@ -823,7 +851,8 @@ def main():
                     help="stack (config 5, the headline) or one config 1-4 case alone (device time only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 1-4 sub-benchmarks")
-    ap.add_argument("--stack-mode", default="chained", choices=["chained", "independent", "launches"])
+    ap.add_argument("--stack-mode", default="auto", choices=["auto", "chained", "independent", "launches"],
+                    help="auto: independent (persistent kernel) at N = 1, launches (chained) at N > 1")
     ap.add_argument("--layers", type=int, default=LAYERS, help="fewer layers only for profiler captures")
     ap.add_argument("--trace", action="store_true", help="record per-linear chain timestamps (gpurun_out/)")
     ap.add_argument("--gemv-timeline", action="store_true",

@@ -47,6 +47,17 @@ def _worker(rank, world, port, outdir):
     wad = torch.from_numpy(np.ascontiguousarray(shard.shard_bytes(wa, NA, world, rank)).view(np.uint8).ravel()).cuda()
     wbd = torch.from_numpy(np.ascontiguousarray(shard.shard_bytes(wb, NB, world, rank)).view(np.uint8).ravel()).cuda()
     xd = torch.from_numpy(x.view(np.uint16).astype(np.int16)).cuda().view(torch.float16)
+    # Load both kernels on this rank before the ranks wait on one another
+    # (lazy module loading of a first launch can delay one rank by more than
+    # the kernels' bounded waits): the same calls at world size 1, locally.
+    lg = GatherGroup(None, 1, 0)
+    la, lb = lg.buffer(NA), lg.buffer(NB)
+    rt.quant_linear_gather(wad.data_ptr(), S.Q4_K, xd.data_ptr(), rt.Y_F16, 1, a1 - a0, KA, KA, a1 - a0, 0,
+                           lg.op(la), 0)
+    rt.quant_linear_gather(wbd.data_ptr(), S.Q8_0, xd.data_ptr(), rt.Y_F16, 1, b1 - b0, KB, KA, b1 - b0, 0,
+                           lg.op(lb), 0)
+    torch.cuda.synchronize()
+    rt.check_kernel_errors()
     gg = GatherGroup(dist, world, rank)
     ya = gg.buffer(NA)
     yb = gg.buffer(NB)

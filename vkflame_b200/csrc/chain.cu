@@ -446,27 +446,39 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
     int k = 0, park_slot = 0;
     uint32_t park_phase = 0;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint8_t *x_have = nullptr;  // plain activation row resident in xs (nullptr: none)
+    bool x_have_q6 = false;
+    int x_r0 = 0, x_r1 = 0;
     for (int li = 0; li < p.n; ++li) {
         const Lin &L = p.lin[li];
-            // The hot fields in registers (every asm "memory" clobber would
-            // otherwise force a reload from global memory).
-            const Geo H = geo(L);
+        // The hot fields in registers (every asm "memory" clobber would
+        // otherwise force a reload from global memory).
+        const Geo H = geo(L);
         const int i0 = first_item(cta, H.I, G), i1 = first_item(cta + 1, H.I, G);
         if (i1 <= i0) continue;
         const bool q6 = H.qt == VKF_DEQUANT_Q6_K, q5 = H.qt == VKF_DEQUANT_Q5_K;
         const int sum_b = q6 ? 96 : 64;
         // Activations of this linear: the runs of the units this CTA's items
         // cover.  The barrier before keeps the previous linear's readers.
+        // Skipped when the previous linear of this CTA quantised the same
+        // plain row, with the same sums layout, over at least these runs.
         const int ua = (i0 % H.S) * H.upi, ue = H.S == 1 ? H.units : std::min(H.units, ((i1 - 1) % H.S + 1) * H.upi);
         const bool all_units = (i1 - i0) >= H.S || i0 / H.S != (i1 - 1) / H.S;
         const int r0 = all_units ? 0 : ua * 8, r1 = all_units ? H.units * 8 : ue * 8;
-        consumer_bar();
-        for (int sb = r0 + threadIdx.x; sb < r1; sb += CW * 32) {
-            uint4 v[4];
-            load_run(L, ep, sb, v, p, li);
-            quantize_run(v, sb, q6, xs, sums);
+        const bool same_x = !L.x_ll && L.X == x_have && q6 == x_have_q6 && r0 >= x_r0 && r1 <= x_r1;
+        if (!same_x) {
+            consumer_bar();
+            for (int sb = r0 + threadIdx.x; sb < r1; sb += CW * 32) {
+                uint4 v[4];
+                load_run(L, ep, sb, v, p, li);
+                quantize_run(v, sb, q6, xs, sums);
+            }
+            consumer_bar();
+            x_have = L.x_ll ? nullptr : L.X;
+            x_have_q6 = q6;
+            x_r0 = r0;
+            x_r1 = r1;
         }
-        consumer_bar();
         if (p.trace && threadIdx.x == 0) atomicMax(&p.trace[2 * li], gtimer());
         const int64_t row_off_a = (int64_t)g * H.row_bytes, row_off_b = (int64_t)(g + 8) * H.row_bytes;
         for (int it = i0; it < i1; ++it, ++n) {
