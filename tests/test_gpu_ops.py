@@ -179,7 +179,7 @@ def test_hip_launch_scale_rms_norm_softmax_binop_rope_get_rows(hip):
     b = rng.standard_normal((6, 512)).astype(np.float32)
     bd = Dev(hip, b)
     assert _launch(hip, "k_bin_bcast<op_mul>", (12, 1, 1), (256, 1, 1), [xd.ptr, bd.ptr, yd.ptr]) == 0
-    assert np.array_equal(yd.get(np.float32), po.binop(1, x, b))
+    assert np.array_equal(yd.get(np.float32), po.binop(1, x, b).ravel())
     # a grid that over-covers (16 x 256 > 3072 values) is clamped to the
     # sources' allocations: nothing is written past 3072 values
     big = Dev(hip, np.full(x.size + 1024, 7.0, np.float32))

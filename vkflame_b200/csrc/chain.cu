@@ -502,11 +502,15 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
                 int u = warp - ubase;
                 if (u < 0) u += CW;
                 if (q6) {
-                    for (; u < nu; u += CW) {
+                    // Rows a multiple of 4 bytes: every lane's unit has the same alignment
+                // (the form must be chosen warp-uniformly around mma.sync); else
+                // the shifted form, which serves either alignment.
+                const bool rows4 = (H.row_bytes & 3) == 0;
+                for (; u < nu; u += CW) {
                         const int unit = u0 + u;
                         const uint8_t *pa = ra + u * 210, *pb = rb + u * 210;
                         const float *sx = reinterpret_cast<const float *>(sums + unit * 96);
-                        if (__all_sync(0xffffffffu, (((uintptr_t)pa | (uintptr_t)pb) & 3) == 0)) StepQ6i::run<true>(pa, pb, xs + unit * 512, g, sx, t, acc);
+                        if (rows4 && (((uintptr_t)pa | (uintptr_t)pb) & 3) == 0) StepQ6i::run<true>(pa, pb, xs + unit * 512, g, sx, t, acc);
                         else StepQ6i::run<false>(pa, pb, xs + unit * 512, g, sx, t, acc);
                     }
                 } else if (q5) {

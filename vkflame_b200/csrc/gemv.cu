@@ -637,11 +637,15 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
                 // Q6_K super-blocks are 210 bytes: a unit's words are 4-byte
                 // aligned or 2 mod 4 by its parity, uniformly across the warp
                 // when rows are a multiple of 4 bytes (K a multiple of 512).
+                // Rows a multiple of 4 bytes: every lane's unit has the same alignment
+                // (the form must be chosen warp-uniformly around mma.sync); else
+                // the shifted form, which serves either alignment.
+                const bool rows4 = (a.row_bytes & 3) == 0;
                 for (; u < nu; u += CW) {
                     const int unit = u0 + u;
                     const uint8_t *pa = ra + u * UB, *pb = rb + u * UB;
                     const float *sx = reinterpret_cast<const float *>(sums + unit * 96);
-                    if (__all_sync(0xffffffffu, (((uintptr_t)pa | (uintptr_t)pb) & 3) == 0)) StepQ6i::run<true>(pa, pb, xs + unit * 512, g, sx, t, acc);
+                    if (rows4 && (((uintptr_t)pa | (uintptr_t)pb) & 3) == 0) StepQ6i::run<true>(pa, pb, xs + unit * 512, g, sx, t, acc);
                     else StepQ6i::run<false>(pa, pb, xs + unit * 512, g, sx, t, acc);
                 }
             } else {
