@@ -510,8 +510,9 @@ __global__ void __launch_bounds__(NT, 1) chain_kernel(const __grid_constant__ Pa
                         const int unit = u0 + u;
                         const uint8_t *pa = ra + u * 210, *pb = rb + u * 210;
                         const float *sx = reinterpret_cast<const float *>(sums + unit * 96);
-                        if (rows4 && (((uintptr_t)pa | (uintptr_t)pb) & 3) == 0) StepQ6i::run<true>(pa, pb, xs + unit * 512, g, sx, t, acc);
-                        else StepQ6i::run<false>(pa, pb, xs + unit * 512, g, sx, t, acc);
+                        if (!rows4) StepQ6i::run<2>(pa, pb, xs + unit * 512, g, sx, t, acc);
+                        else if ((((uintptr_t)pa | (uintptr_t)pb) & 3) == 0) StepQ6i::run<0>(pa, pb, xs + unit * 512, g, sx, t, acc);
+                        else StepQ6i::run<1>(pa, pb, xs + unit * 512, g, sx, t, acc);
                     }
                 } else if (q5) {
                     for (; u < nu; u += CW) {

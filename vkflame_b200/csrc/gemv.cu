@@ -645,8 +645,9 @@ __global__ void __launch_bounds__(32 * (CW + 2), CPS) gemv_kernel(const __grid_c
                     const int unit = u0 + u;
                     const uint8_t *pa = ra + u * UB, *pb = rb + u * UB;
                     const float *sx = reinterpret_cast<const float *>(sums + unit * 96);
-                    if (rows4 && (((uintptr_t)pa | (uintptr_t)pb) & 3) == 0) StepQ6i::run<true>(pa, pb, xs + unit * 512, g, sx, t, acc);
-                    else StepQ6i::run<false>(pa, pb, xs + unit * 512, g, sx, t, acc);
+                    if (!rows4) StepQ6i::run<2>(pa, pb, xs + unit * 512, g, sx, t, acc);
+                        else if ((((uintptr_t)pa | (uintptr_t)pb) & 3) == 0) StepQ6i::run<0>(pa, pb, xs + unit * 512, g, sx, t, acc);
+                        else StepQ6i::run<1>(pa, pb, xs + unit * 512, g, sx, t, acc);
                 }
             } else {
                 for (; u < nu; u += CW) unit_step(u);

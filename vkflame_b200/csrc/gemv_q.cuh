@@ -444,13 +444,19 @@ template <bool Q5> struct StepK1i {
 // (x = s_j * (256 xh + xl) per 32-value run j = 4 ip + s); thread (g, t) owns
 // groups (ip, t, h) and adds  d * sc * (s_j * (256 Dh + Dl) - 32 * X16).
 // Odd super-blocks start 2 mod 4: their words are two aligned words and a
-// funnel shift (AL4 = false, which serves any 2-byte alignment, so the choice
-// can be made warp-uniform: mma.sync must be executed by the whole warp).
+// byte permute (AL4 = 1); rows of 2 mod 4 bytes mix both within a warp and
+// take the lane-by-lane form (AL4 = 2): mma.sync must be executed by the
+// whole warp, so the form is chosen warp-uniformly.
 struct StepQ6i {
-    template <bool AL4> __device__ __forceinline__ static uint32_t w32(const uint8_t *p) {
-        if constexpr (AL4) return *reinterpret_cast<const uint32_t *>(p);
-        // Any 2-byte aligned address (lanes of one warp may differ): the two
-        // aligned words around it, shifted by 0 or 16 bits.
+    // AL: 0 the address is 4-byte aligned; 1 it is 2 mod 4 (two aligned
+    // words and a byte permute); 2 either, lane by lane (a funnel shift by
+    // the address: rows of 2 mod 4 bytes, where lanes of one warp differ).
+    template <int AL> __device__ __forceinline__ static uint32_t w32(const uint8_t *p) {
+        if constexpr (AL == 0) return *reinterpret_cast<const uint32_t *>(p);
+        if constexpr (AL == 1) {
+            const uint32_t lo = *reinterpret_cast<const uint32_t *>(p - 2), hi = *reinterpret_cast<const uint32_t *>(p + 2);
+            return prmt(lo, hi, 0x5432);
+        }
         const uintptr_t a = (uintptr_t)p;
         const uint32_t *q = reinterpret_cast<const uint32_t *>(a & ~(uintptr_t)3);
         return __funnelshift_r(q[0], q[1], (uint32_t)(a & 3) * 8);
@@ -462,7 +468,7 @@ struct StepQ6i {
         return lop3_and_or(hs, 0x30303030u, nib);
     }
     // xu: the unit's xh[256] | xl[256]; sx: s[8] (runs) | X16[16] (groups).
-    template <bool AL4>
+    template <int AL4>
     __device__ __forceinline__ static void run(const uint8_t *ra, const uint8_t *rb, const uint8_t *xu, int g,
                                                const float *sx, int t, float (&acc)[4]) {
         const float da = half_bits_to_float(ld_u16(ra + 208)), db = half_bits_to_float(ld_u16(rb + 208));
