@@ -235,15 +235,11 @@ class Stack:
     vkflame_quant_linear_gather launch per linear (N = 1: independent
     vkflame_quant_linear_ex launches), for comparison."""
 
-    def __init__(self, world, rank, dist, stream, mode="chained", trace=False, layers=None, v_side=True):
+    def __init__(self, world, rank, dist, stream, mode="chained", trace=False, layers=None):
         import torch
         from vkflame_b200 import rt, shard
         from vkflame_b200.gather import GatherGroup
         self.rt, self.world, self.rank, self.dist, self.stream, self.mode = rt, world, rank, dist, stream, mode
-        self.v_side = v_side and mode == "launches"
-        if self.v_side:
-            self.side = torch.cuda.Stream()
-            self.ev_fork, self.ev_join = torch.cuda.Event(), torch.cuda.Event()
         # Chained forms: a small input row (N(0,1) x 1e-6) so that the first
         # layer's outputs stay finite in fp16 (with these random weights each
         # link multiplies the magnitudes by ~100) and can be checked; the
@@ -303,24 +299,11 @@ class Stack:
         if self.chain is not None:
             self.chain.run(self.stream)
             return
-        import torch
         rt = self.rt
-        # v's output feeds no later linear, so its launches go to a side
-        # stream (forked from and joined to the token's stream): they are off
-        # the chain of dependent launches.  Its input words are validated
-        # inside the kernel, so it needs no stream dependency on down.
-        side = self.side if self.v_side else None
-        if side is not None:
-            self.ev_fork.record(torch.cuda.current_stream())
-            side.wait_event(self.ev_fork)
         for q, K, n, w, x, y, g, name in self.ops:
             ldx = x.shape[2] * 2 if g.x_gathered else x.shape[1]  # gathered X: words of 2 values
-            st = side.cuda_stream if (side is not None and name == "v") else self.stream
             rt.quant_linear_gather(w.data_ptr(), q, x.data_ptr(), rt.Y_F16, 1, n, K, ldx, y.N,
-                                   rt.FLAG_STATIC_WEIGHTS, g, st)
-        if side is not None:
-            self.ev_join.record(side)
-            torch.cuda.current_stream().wait_event(self.ev_join)
+                                   rt.FLAG_STATIC_WEIGHTS, g, self.stream)
 
     def runs(self) -> int:
         """Completed runs (the chain's epoch; "launches": the first call site's)."""
@@ -412,8 +395,7 @@ def run_stack(args, world, rank, local, dist, mode, steps, e2e=True, trace=False
     s = torch.cuda.Stream()
     res = {}
     with torch.cuda.stream(s):
-        st = Stack(world, rank, dist, s.cuda_stream, mode=mode, trace=trace, layers=args.layers,
-                   v_side=not args.no_v_side)
+        st = Stack(world, rank, dist, s.cuda_stream, mode=mode, trace=trace, layers=args.layers)
         st.step()  # one-time setup outside the capture
         torch.cuda.synchronize()
         l0 = rt.launch_count()
@@ -872,7 +854,6 @@ def main():
     ap.add_argument("--stack-mode", default="auto", choices=["auto", "chained", "independent", "launches"],
                     help="auto: independent (persistent kernel) at N = 1, launches (chained) at N > 1")
     ap.add_argument("--layers", type=int, default=LAYERS, help="fewer layers only for profiler captures")
-    ap.add_argument("--no-v-side", action="store_true", help="launches mode: keep v on the token's stream")
     ap.add_argument("--trace", action="store_true", help="record per-linear chain timestamps (gpurun_out/)")
     ap.add_argument("--gemv-timeline", action="store_true",
                     help="with --stack-mode launches and the diagnostic build (make -C vkflame_b200/csrc timing; "

@@ -78,7 +78,7 @@ template <> struct Packed<VKF_DEQUANT_Q4_K> { static constexpr int RB = 144; };
 template <> struct Packed<VKF_DEQUANT_Q5_K> { static constexpr int RB = 176; };
 // Q6_K: 210 packed bytes per row and 256 values, so row pitches are not
 // 16-byte multiples and no tensor map describes the rows.  Each row's 210
-// bytes are fetched with its own bulk copy from the 16-byte boundary below
+// bytes are fetched as 16-byte cp.async granules from the boundary below
 // them (at most 224 bytes) into a 240-byte slot (15 granules: odd, so eight
 // consecutive rows' 16-byte loads hit eight distinct bank groups); the
 // converter reads the row at the slot + its start's offset mod 16.
@@ -440,7 +440,7 @@ __global__ void __launch_bounds__(NT, 1)
             mbar_init(&ab_empty[s], 1);
         }
         for (int s = 0; s < RS; ++s) {
-            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_full[s], row_copies<QT>() ? 32 : 1);  // row copies: one arrival per producer lane
             mbar_init(&raw_empty[s], CV);
         }
         for (int b = 0; b < 2; ++b) {
@@ -491,8 +491,10 @@ __global__ void __launch_bounds__(NT, 1)
         // ---- packed weight bytes: one tensor copy per 128 rows x 256 values ----
         if (!p.prefetch) asm volatile("griddepcontrol.wait;" ::: "memory");
         if constexpr (row_copies<QT>()) {
-            // one bulk copy per row (4 rows per lane), 16-byte aligned source
-            // and size; the transaction count is the warp's byte total
+            // 16-byte cp.async granules (4 rows per lane, at most 14 granules
+            // from the boundary below each row's start): one bulk copy per row
+            // held the stage to the TMA unit's operation rate.  Each lane
+            // arrives on the stage barrier (count 32) when its copies land.
             int g = 0;
             bool ok = true;
             for (int u = u_begin; u < u_end && ok;) {
@@ -502,28 +504,21 @@ __global__ void __launch_bounds__(NT, 1)
                 for (int kr = sg.kr0; kr < sg.kr1; ++kr, ++g) {
                     const int s = g % RS;
                     if (g >= RS && !(ok = mbar_wait(&raw_empty[s], ((g / RS) & 1) ^ 1, p.err))) break;
-                    const uint8_t *src[4];
-                    uint32_t sz[4], total = 0;
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int r = lane + 32 * i;
-                        sz[i] = 0;
-                        src[i] = nullptr;
-                        if (n0 + r < p.N) {
-                            const uint8_t *q = p.W + (int64_t)(n0 + r) * p.row_bytes + (int64_t)kr * Q6_ROW;
-                            const uint32_t mis = (uint32_t)((uintptr_t)q & 15);
-                            src[i] = q - mis;
-                            sz[i] = (mis + Q6_ROW + 15) & ~15u;
-                            total += sz[i];
-                        }
+                        if (n0 + r >= p.N) continue;
+                        const uint8_t *q = p.W + (int64_t)(n0 + r) * p.row_bytes + (int64_t)kr * Q6_ROW;
+                        const uint32_t mis = (uint32_t)((uintptr_t)q & 15);
+                        const uint8_t *src = q - mis;
+                        const uint32_t dst = smem_addr(raw + s * RAW_BYTES + r * RB);
+                        const int ng = (int)((mis + Q6_ROW + 15) >> 4);
+                        for (int j = 0; j < ng; ++j)
+                            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + 16 * j), "l"(src + 16 * j)
+                                         : "memory");
                     }
-#pragma unroll
-                    for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-                    if (lane == 0) mbar_arrive_expect_tx(&raw_full[s], total);
-                    __syncwarp();
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        if (sz[i]) bulk_g2s(raw + s * RAW_BYTES + (lane + 32 * i) * RB, src[i], sz[i], &raw_full[s]);
+                    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(&raw_full[s]))
+                                 : "memory");
                 }
             }
         } else if (lane == 0) {
