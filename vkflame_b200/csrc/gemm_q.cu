@@ -329,11 +329,13 @@ __device__ __forceinline__ void lds32_at(const uint8_t *slot, int p, uint32_t (&
 
 // Q6_K (dequant_q6_k.glsl:28-58), the 32 values of sub-block B (ip = B / 4,
 // s = B % 4): code q = nibble of ql[64 ip + 32 (s & 1) + l] (low for s < 2)
-// | bits 2s, 2s + 1 of qh[32 ip + l] << 4; value = d * float(sc * (q - 32))
-// with sc = scales[8 ip + 2 s + l / 16].  sc * (q - 32) is an exact integer
-// and its product with the fp16 d is exact in fp32 (24 bits), so the one
-// rounding is to fp16: the shader's value rounded once.  row: the row's slot;
-// off: the row's first byte within it.
+// | bits 2s, 2s + 1 of qh[32 ip + l] << 4; value = d * sc * (q - 32) with
+// sc = scales[8 ip + 2 s + l / 16].  In half2: (1024 + q) - 1056 = q - 32
+// exactly, times sc (exact unless |sc (q - 32)| > 2048 and odd: one
+// rounding of at most 2^-12 relative), times d (one rounding).  The fp32 form
+// (exact product, one rounding) took three times the instructions and held
+// the prefill to a third of the Q4_K rate.  row: the row's slot; off: the
+// row's first byte within it.
 template <int B>
 __device__ __forceinline__ void convert32_q6(const uint8_t *row, int off, uint32_t (&o)[16]) {
     constexpr int IP = B / 4, S = B % 4;
@@ -341,19 +343,18 @@ __device__ __forceinline__ void convert32_q6(const uint8_t *row, int off, uint32
     lds32_at(row, off + 64 * IP + 32 * (S & 1), ql);
     lds32_at(row, off + 128 + 32 * IP, qh);
     const uint32_t scw = *reinterpret_cast<const uint16_t *>(row + off + 192 + 8 * IP + 2 * S);
-    const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(row + off + 208)));
-    const float sc0 = (float)(int8_t)(scw & 0xFF), sc1 = (float)(int8_t)(scw >> 8);
+    const __half2 d2 = __half2half2(__ushort_as_half(*reinterpret_cast<const uint16_t *>(row + off + 208)));
+    const __half2 sc0 = __float2half2_rn((float)(int8_t)(scw & 0xFF)), sc1 = __float2half2_rn((float)(int8_t)(scw >> 8));
+    const __half2 off2 = __float2half2_rn(1056.0f);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const uint32_t nib = (S >= 2 ? ql[j] >> 4 : ql[j]) & 0x0F0F0F0Fu;
         const uint32_t c = nib | (((qh[j] >> (2 * S)) & 0x03030303u) << 4);
-        const float sc = j < 4 ? sc0 : sc1;
-        float f[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e)  // 2^23 + code, exact; minus 2^23 + 32: code - 32, exact
-            f[e] = d * (sc * (__uint_as_float(__byte_perm(c, 0x4B000000u, 0x7650u | e)) - 8388640.0f));
-        o[2 * j] = h2u(__floats2half2_rn(f[0], f[1]));
-        o[2 * j + 1] = h2u(__floats2half2_rn(f[2], f[3]));
+        const __half2 sc = j < 4 ? sc0 : sc1;
+        const __half2 q01 = __hsub2(u2h(__byte_perm(c, 0x64646464u, 0x5140)), off2);
+        const __half2 q23 = __hsub2(u2h(__byte_perm(c, 0x64646464u, 0x7362)), off2);
+        o[2 * j] = h2u(__hmul2(__hmul2(q01, sc), d2));
+        o[2 * j + 1] = h2u(__hmul2(__hmul2(q23, sc), d2));
     }
 }
 
