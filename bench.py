@@ -691,10 +691,33 @@ def bench_prefill_stack(M=512):
     torch.cuda.empty_cache()
     return {"ms": ms, "TFLOP/s": flops / (ms * 1e-3) / 1e12, "tflop_per_step": flops / 1e12,
             "weight_gb": wbytes / 1e9, "roofline": tensor_roofline(flops, ms, "f16"),
-            "note": "Q6_K links (attn_v, ffn_down, head) widen W to fp16 in scratch before the GEMM"}
+            "note": "every link on the fused-dequant tcgen05 prefill (Q4_K and Q6_K)"}
+
+
+# Prefill GEMMs of the stack's shapes at M = 512 (config 5's components).
+PREFILL_CASES = {"prefill_q4K_gate_up_M512": (S.Q4_K, 5120, 27648, 512),
+                 "prefill_q6K_down_M512": (S.Q6_K, 13824, 5120, 512),
+                 "prefill_q6K_head_M512": (S.Q6_K, 5120, 152064, 512)}
+
+
+def bench_prefill_case(name):
+    """One fused-dequant prefill GEMM (vkflame_quant_linear_ex, M = 512)."""
+    import torch
+    from vkflame_b200 import rt
+    q, K, N, M = PREFILL_CASES[name]
+    w = make_quant_weight_gpu(q, N, K, 5)
+    x = torch.randn((M, K), device="cuda").half()
+    y = torch.empty((M, N), device="cuda", dtype=torch.float16)
+    def fn(sp):
+        rt.quant_linear_ex(w.data_ptr(), q, x.data_ptr(), rt.X_F16, y.data_ptr(), rt.Y_F16, M, N, K, K, N,
+                           rt.FLAG_STATIC_WEIGHTS, sp)
+    ms = graph_time(fn, iters=3 if N > 100000 else 10)
+    flops = 2 * M * N * K
+    return {"us": ms * 1e3, "TFLOP/s": flops / (ms * 1e-3) / 1e12, "roofline": tensor_roofline(flops, ms, "f16")}
 
 
 SUB_CASES = dict({n: (lambda n=n: bench_gemv_case(n)) for n in GEMV_CASES},
+                 **{n: (lambda n=n: bench_prefill_case(n)) for n in PREFILL_CASES},
                  config2_int8_linear_M512=bench_int8_linear, config4_q8_0_x_q8_1_M512=bench_q8_prefill,
                  config5_prefill_stack_M512=bench_prefill_stack)
 

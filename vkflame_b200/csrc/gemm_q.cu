@@ -48,6 +48,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <climits>
 #include <type_traits>
@@ -111,6 +112,7 @@ struct Params {
     unsigned *err;
     const uint8_t *W; // the ggml rows (row-copy formats)
     int64_t row_bytes;
+    int q6_bulk;      // row-copy formats: one bulk copy per row instead of cp.async granules
 };
 
 // Segment walk shared by every role: CTA c owns units [u0, u1); a segment is
@@ -318,11 +320,16 @@ __device__ __forceinline__ void lds32_at(const uint8_t *slot, int p, uint32_t (&
     const uint4 a0 = *reinterpret_cast<const uint4 *>(b), a1 = *reinterpret_cast<const uint4 *>(b + 16),
                 a2 = *reinterpret_cast<const uint4 *>(b + 32);
     const uint32_t w[12] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w, a2.x, a2.y, a2.z, a2.w};
-    const int ws = (p >> 2) & 3;
+    // The word offset differs from lane to lane (rows start at different
+    // offsets): two levels of predicated selects, no branches (a four-way
+    // choice compiled to divergent branches and stalled the converters).
+    const bool s2 = (p & 8) != 0, s1 = (p & 4) != 0;
     const uint32_t sh = (uint32_t)(p & 3) * 8;
-    uint32_t v[9];
+    uint32_t t[10], v[9];
 #pragma unroll
-    for (int j = 0; j < 9; ++j) v[j] = ws == 0 ? w[j] : ws == 1 ? w[j + 1] : ws == 2 ? w[j + 2] : w[j + 3];
+    for (int j = 0; j < 10; ++j) t[j] = s2 ? w[j + 2] : w[j];
+#pragma unroll
+    for (int j = 0; j < 9; ++j) v[j] = s1 ? t[j + 1] : t[j];
 #pragma unroll
     for (int j = 0; j < 8; ++j) out[j] = __funnelshift_r(v[j], v[j + 1], sh);
 }
@@ -505,6 +512,32 @@ __global__ void __launch_bounds__(NT, 1)
                 for (int kr = sg.kr0; kr < sg.kr1; ++kr, ++g) {
                     const int s = g % RS;
                     if (g >= RS && !(ok = mbar_wait(&raw_empty[s], ((g / RS) & 1) ^ 1, p.err))) break;
+                    if (p.q6_bulk) {
+                        // one bulk copy per row; lane 0 states the stage's bytes,
+                        // every lane arrives after issuing its copies
+                        uint32_t tot = 0;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int r = lane + 32 * i;
+                            if (n0 + r >= p.N) continue;
+                            const uintptr_t q = (uintptr_t)(p.W + (int64_t)(n0 + r) * p.row_bytes + (int64_t)kr * Q6_ROW);
+                            tot += ((uint32_t)(q & 15) + Q6_ROW + 15) & ~15u;
+                        }
+#pragma unroll
+                        for (int o = 16; o; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+                        if (lane == 0) mbar_expect_tx(&raw_full[s], tot);
+                        __syncwarp();
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int r = lane + 32 * i;
+                            if (n0 + r >= p.N) continue;
+                            const uint8_t *q = p.W + (int64_t)(n0 + r) * p.row_bytes + (int64_t)kr * Q6_ROW;
+                            const uint32_t mis = (uint32_t)((uintptr_t)q & 15);
+                            bulk_g2s(raw + s * RAW_BYTES + r * RB, q - mis, (mis + Q6_ROW + 15) & ~15u, &raw_full[s]);
+                        }
+                        mbar_arrive(&raw_full[s]);
+                        continue;
+                    }
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int r = lane + 32 * i;
@@ -855,7 +888,10 @@ struct Cfg {
     // Deepest A/B ring (<= 4) that still leaves RSMIN packed stages (a
     // packed stage feeds four K-blocks; three instead of two measured no
     // different), then as many packed stages (<= 6) as fit.
-    static constexpr int NSF = (SMEM_CAP - FIXED - VKF_QGEMM_RSMIN * RAW_BYTES) / STAGE;
+    // Row-copy formats (Q6_K) keep three packed stages: their per-row
+    // granule fetches have a longer latency per stage than one tensor copy.
+    static constexpr int RSMIN = row_copies<QT>() ? 3 : VKF_QGEMM_RSMIN;
+    static constexpr int NSF = (SMEM_CAP - FIXED - RSMIN * RAW_BYTES) / STAGE;
     static constexpr int NS = NSF >= VKF_QGEMM_NSMAX ? VKF_QGEMM_NSMAX : NSF;
     static constexpr int RS0 = (SMEM_CAP - FIXED - NS * STAGE) / RAW_BYTES;
     static constexpr int RS = RS0 > 6 ? 6 : RS0;
@@ -917,7 +953,12 @@ static int launch(const void *W, const void *X, int64_t ldx, void *Y, int y_f16,
     memset(&ty, 0, sizeof(ty));
     const int esize = y_f16 ? 2 : 4;
     const int y_tma = make_rowmajor_map(&ty, Y, esize, M, N, ldy, BW, 32) ? 1 : 0;
-    Params p{M, N, K, Y, ldy, y_f16, y_tma, prefetch, units, ws, flags, ds->d_error, (const uint8_t *)W, row_bytes};
+    static const int q6_bulk = [] {
+        const char *e = getenv("VKFLAME_Q6_FETCH");
+        return e && e[0] == 'b' ? 1 : 0;
+    }();
+    Params p{M, N, K, Y, ldy, y_f16, y_tma, prefetch, units, ws, flags, ds->d_error, (const uint8_t *)W, row_bytes,
+             q6_bulk};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(NT);
