@@ -112,7 +112,6 @@ struct Params {
     unsigned *err;
     const uint8_t *W; // the ggml rows (row-copy formats)
     int64_t row_bytes;
-    int q6_bulk;      // row-copy formats: one bulk copy per row instead of cp.async granules
 };
 
 // Segment walk shared by every role: CTA c owns units [u0, u1); a segment is
@@ -501,7 +500,8 @@ __global__ void __launch_bounds__(NT, 1)
         if constexpr (row_copies<QT>()) {
             // 16-byte cp.async granules (4 rows per lane, at most 14 granules
             // from the boundary below each row's start): one bulk copy per row
-            // held the stage to the TMA unit's operation rate.  Each lane
+            // measured 1.5x slower (the TMA unit's operation rate at 224-byte
+            // copies).  Each lane
             // arrives on the stage barrier (count 32) when its copies land.
             int g = 0;
             bool ok = true;
@@ -512,32 +512,6 @@ __global__ void __launch_bounds__(NT, 1)
                 for (int kr = sg.kr0; kr < sg.kr1; ++kr, ++g) {
                     const int s = g % RS;
                     if (g >= RS && !(ok = mbar_wait(&raw_empty[s], ((g / RS) & 1) ^ 1, p.err))) break;
-                    if (p.q6_bulk) {
-                        // one bulk copy per row; lane 0 states the stage's bytes,
-                        // every lane arrives after issuing its copies
-                        uint32_t tot = 0;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const int r = lane + 32 * i;
-                            if (n0 + r >= p.N) continue;
-                            const uintptr_t q = (uintptr_t)(p.W + (int64_t)(n0 + r) * p.row_bytes + (int64_t)kr * Q6_ROW);
-                            tot += ((uint32_t)(q & 15) + Q6_ROW + 15) & ~15u;
-                        }
-#pragma unroll
-                        for (int o = 16; o; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-                        if (lane == 0) mbar_expect_tx(&raw_full[s], tot);
-                        __syncwarp();
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const int r = lane + 32 * i;
-                            if (n0 + r >= p.N) continue;
-                            const uint8_t *q = p.W + (int64_t)(n0 + r) * p.row_bytes + (int64_t)kr * Q6_ROW;
-                            const uint32_t mis = (uint32_t)((uintptr_t)q & 15);
-                            bulk_g2s(raw + s * RAW_BYTES + r * RB, q - mis, (mis + Q6_ROW + 15) & ~15u, &raw_full[s]);
-                        }
-                        mbar_arrive(&raw_full[s]);
-                        continue;
-                    }
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int r = lane + 32 * i;
@@ -953,12 +927,7 @@ static int launch(const void *W, const void *X, int64_t ldx, void *Y, int y_f16,
     memset(&ty, 0, sizeof(ty));
     const int esize = y_f16 ? 2 : 4;
     const int y_tma = make_rowmajor_map(&ty, Y, esize, M, N, ldy, BW, 32) ? 1 : 0;
-    static const int q6_bulk = [] {
-        const char *e = getenv("VKFLAME_Q6_FETCH");
-        return e && e[0] == 'b' ? 1 : 0;
-    }();
-    Params p{M, N, K, Y, ldy, y_f16, y_tma, prefetch, units, ws, flags, ds->d_error, (const uint8_t *)W, row_bytes,
-             q6_bulk};
+    Params p{M, N, K, Y, ldy, y_f16, y_tma, prefetch, units, ws, flags, ds->d_error, (const uint8_t *)W, row_bytes};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(NT);
