@@ -445,6 +445,82 @@ def run_stack(args, world, rank, local, dist, mode, steps, e2e=True, trace=False
     return res
 
 
+def e2e_through_hip(steps=20, warmup=3):
+    """The N = 1 weight-streaming token through the reference's own API, as
+    ggml-hip drives it: the layer input row as Q8_1 blocks copied in with
+    hipMemcpyAsync, one hipLaunchKernel("mul_mat_<fmt>_q8_1") per linear
+    (libamdhip64 drop-in -> vkflame_quant_linear, fp32 outputs), the head's
+    fp32 logits copied out with hipMemcpyAsync; timed with hipEvents, host
+    launches included (no CUDA graph)."""
+    import ctypes as C
+    import torch
+    from vkflame_b200 import LIBS, rt
+    hip = C.CDLL(str(LIBS["hip"]))
+
+    class Dim3(C.Structure):
+        _fields_ = [("x", C.c_uint), ("y", C.c_uint), ("z", C.c_uint)]
+    hip.hipLaunchKernel.argtypes = [C.c_void_p, Dim3, Dim3, C.POINTER(C.c_void_p), C.c_size_t, C.c_void_p]
+    hip.__hipRegisterFunction.argtypes = [C.c_void_p, C.c_void_p, C.c_char_p, C.c_char_p, C.c_int] + [C.c_void_p] * 5
+    hip.hipMemcpyAsync.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_void_p]
+    hip.hipEventRecord.argtypes = [C.c_void_p, C.c_void_p]
+    hip.hipEventElapsedTime.argtypes = [C.POINTER(C.c_float), C.c_void_p, C.c_void_p]
+    hip.hipStreamSynchronize.argtypes = [C.c_void_p]
+    stubs, names = [], {}
+    for fmt, nm in ((S.Q4_K, "mul_mat_q4_K_q8_1"), (S.Q6_K, "mul_mat_q6_K_q8_1")):
+        stub = C.create_string_buffer(8)
+        stubs.append(stub)
+        hip.__hipRegisterFunction(None, C.addressof(stub), nm.encode(), nm.encode(), -1, None, None, None, None, None)
+        names[fmt] = C.addressof(stub)
+    links = stack_links()
+    xs = {K: torch.randn((1, K), device="cuda") for K in (HIDDEN, FFN)}
+    xq = {K: torch.empty(K // 32 * 36, dtype=torch.uint8, device="cuda") for K in (HIDDEN, FFN)}
+    for K in xq:
+        rt.quantize_q8_1(xs[K].data_ptr(), xq[K].data_ptr(), 1, K, K)
+    xq_host = {K: xq[K].cpu().pin_memory() for K in xq}
+    ws, ys = [], {}
+    for i, (name, q, K, N, inp) in enumerate(links):
+        ws.append(make_quant_weight_gpu(q, N, K, link_seed(0, i)))
+        ys.setdefault(N, torch.empty(N, device="cuda"))
+    out_host = torch.empty(VOCAB).pin_memory()
+    stream, e0, e1 = C.c_void_p(), C.c_void_p(), C.c_void_p()
+    assert hip.hipStreamCreate(C.byref(stream)) == 0
+    hip.hipEventCreateWithFlags(C.byref(e0), 0)
+    hip.hipEventCreateWithFlags(C.byref(e1), 0)
+    holders = []
+
+    def launch_token():
+        for K in xq:  # ggml's activation row, Q8_1, host -> device
+            assert hip.hipMemcpyAsync(C.c_void_p(xq[K].data_ptr()), C.c_void_p(xq_host[K].data_ptr()),
+                                      xq[K].numel(), 1, stream) == 0
+        for i, (name, q, K, N, inp) in enumerate(links):
+            a = [C.c_void_p(ws[i].data_ptr()), C.c_void_p(xq[K].data_ptr()), C.c_void_p(ys[N].data_ptr()),
+                 C.c_int(K), C.c_int(N), C.c_int(K), C.c_int(1), C.c_int(N)]
+            holders[:] = a
+            argv = (C.c_void_p * len(a))(*[C.addressof(h) for h in a])
+            assert hip.hipLaunchKernel(C.c_void_p(names[q]), Dim3(1, 1, 1), Dim3(32, 1, 1), argv, 0, stream) == 0
+        assert hip.hipMemcpyAsync(C.c_void_p(out_host.data_ptr()), C.c_void_p(ys[VOCAB].data_ptr()), VOCAB * 4, 2,
+                                  stream) == 0
+    for _ in range(warmup):
+        launch_token()
+    hip.hipStreamSynchronize(stream)
+    hip.hipEventRecord(e0, stream)
+    for _ in range(steps):
+        launch_token()
+    hip.hipEventRecord(e1, stream)
+    hip.hipStreamSynchronize(stream)
+    ms = C.c_float()
+    hip.hipEventElapsedTime(C.byref(ms), e0, e1)
+    per = ms.value / steps
+    nbytes = sum(w.numel() for w in ws)
+    rt.check_kernel_errors()
+    del ws
+    torch.cuda.empty_cache()
+    return {"value": nbytes / (per * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": per,
+            "h2d_bytes_per_step": sum(v.numel() for v in xq.values()), "d2h_bytes_per_step": VOCAB * 4,
+            "path": "libamdhip64: hipMemcpyAsync + 241 x hipLaunchKernel(mul_mat_*_q8_1) + hipMemcpyAsync, "
+                    "no CUDA graph (host launch rate included)"}
+
+
 def bench_stack(args, world, rank, local, dist):
     """The headline.  Default (--stack-mode auto): at N = 1 the stack's
     weight-streaming figure, every linear reading its layer input, as one
@@ -468,6 +544,7 @@ def bench_stack(args, world, rank, local, dist):
             extra[f"{alt}_ms_per_token"] = r["ms"]
             extra[f"{alt}_gb_s"] = r["weight_bytes"] / (r["ms"] * 1e-3) / 1e9
             extra[f"{alt}_parity"] = r["parity"]
+        extra["e2e_through_hip"] = e2e_through_hip()
     ms, ems = res["ms"], res["e2e_ms"]
     weight_bytes = res["weight_bytes"]
     total_bytes = weight_bytes * world  # every rank streams its shard once per token
