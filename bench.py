@@ -544,7 +544,8 @@ def bench_stack(args, world, rank, local, dist):
             extra[f"{alt}_ms_per_token"] = r["ms"]
             extra[f"{alt}_gb_s"] = r["weight_bytes"] / (r["ms"] * 1e-3) / 1e9
             extra[f"{alt}_parity"] = r["parity"]
-        extra["e2e_through_hip"] = e2e_through_hip()
+        if args.e2e_hip:
+            extra["e2e_through_hip"] = e2e_through_hip()
     ms, ems = res["ms"], res["e2e_ms"]
     weight_bytes = res["weight_bytes"]
     total_bytes = weight_bytes * world  # every rank streams its shard once per token
@@ -588,8 +589,8 @@ def bench_stack(args, world, rank, local, dist):
         "gpu_launches": res["launches_per_step"] * args.steps, "clocks": res["clocks"],
     }
     if "trace" in res:
-        out = ROOT / "gpurun_out"
-        out.mkdir(exist_ok=True)
+        out = Path(args.trace)
+        out.mkdir(parents=True, exist_ok=True)
         np.save(out / f"chain_trace_w{world}_r{rank}.npy", res["trace"])
     return line
 
@@ -954,12 +955,20 @@ def main():
     ap.add_argument("--stack-mode", default="auto", choices=["auto", "chained", "independent", "launches"],
                     help="auto: independent (persistent kernel) at N = 1, launches (chained) at N > 1")
     ap.add_argument("--layers", type=int, default=LAYERS, help="fewer layers only for profiler captures")
-    ap.add_argument("--trace", action="store_true", help="record per-linear chain timestamps (gpurun_out/)")
+    ap.add_argument("--e2e-hip", action="store_true",
+                    help="N = 1: also time the token through libamdhip64 (hipLaunchKernel per linear)")
+    ap.add_argument("--watchdog", type=float, default=0,
+                    help="dump every thread's Python stack and exit after this many seconds (0: off)")
+    ap.add_argument("--trace", default=None, metavar="DIR",
+                    help="record per-linear chain timestamps; saved as DIR/chain_trace_w<N>_r<rank>.npy")
     ap.add_argument("--gemv-timeline", action="store_true",
                     help="with --stack-mode launches and the diagnostic build (make -C vkflame_b200/csrc timing; "
                          "VKFLAME_RT_LIB=vkflame_b200/lib/timing/libvkflame_rt.so): per-launch and per-CTA "
                          "timestamps of one token, summarised on stdout")
     args = ap.parse_args()
+    if args.watchdog > 0:
+        import faulthandler
+        faulthandler.dump_traceback_later(args.watchdog, exit=True)
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_env()
 
