@@ -82,6 +82,8 @@ int blas_gemm_ex(int transA, int transB, int m, int n, int k, float alpha, const
     const size_t a2bytes = ((size_t)n * kp * es + 255) & ~size_t(255);
     const size_t b2bytes = ((size_t)m * kp * es + 255) & ~size_t(255);
     const bool split = atype == BT_F32 && ctype == BT_F32;
+    if (atype != BT_I8 && (row_scale || col_scale)) return VKF_ERR_UNSUPPORTED;
+    if (atype == BT_I8 && (alpha != 1.0f || beta != 0.0f)) return VKF_ERR_UNSUPPORTED;
     uint8_t *scr = (uint8_t *)stream_scratch(stream, (a2bytes + b2bytes) * (split ? 3 : 1));
     if (!scr) return VKF_ERR_NOMEM;
     // A'' (n x k) from B: K-major iff op(B) = B (column-major k x n = row-major n x k).
@@ -100,9 +102,9 @@ int blas_gemm_ex(int transA, int transB, int m, int n, int k, float alpha, const
         // (~2^-22 relative) is dropped.
         float *ah = (float *)(scr + a2bytes + b2bytes), *al = (float *)((uint8_t *)ah + a2bytes);
         float *bh = (float *)((uint8_t *)al + a2bytes), *bl = (float *)((uint8_t *)bh + b2bytes);
+        if (row_scale || col_scale) return VKF_ERR_UNSUPPORTED;
         if ((rc = split_tf32((const float *)a2, lda2, ah, al, kp, n, k, stream))) return rc;
         if ((rc = split_tf32((const float *)b2, ldb2, bh, bl, kp, m, k, stream))) return rc;
-        if (row_scale || col_scale) return VKF_ERR_UNSUPPORTED;
         if ((rc = gemm_tf32_tn(al, kp, bh, kp, n, m, k, alpha, beta, beta != 0.0f ? C : nullptr, ldc, 0, nullptr, 0,
                                C, ldc, 0, stream)))
             return rc;
