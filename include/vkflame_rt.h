@@ -253,6 +253,7 @@ int vkflame_linear_int8(const int8_t *X, const int8_t *W, const float *sx, const
  * stream, set with vkflame_set_stream (NULL, the default: the legacy
  * default stream).  vkflame_set_stream has no reference counterpart. */
 int vkflame_set_stream(void *stream);
+void *vkflame_get_stream(void);   /* the calling thread's stream for these entry points */
 /* VKF_EW_* op ids of runtime/dispatch.h:24-38 (kernels/elementwise_f32.glsl). */
 #define VKF_EW_SILU 0
 #define VKF_EW_GELU_ERF 1

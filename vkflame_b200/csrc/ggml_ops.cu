@@ -312,6 +312,8 @@ extern "C" int vkflame_set_stream(void *stream) {
     return set_status(VKF_OK);
 }
 
+extern "C" void *vkflame_get_stream(void) { return (void *)ops::t_stream; }
+
 extern "C" int vkflame_dispatch_elementwise_f32(void *ctx, const void *src, void *dst, uint32_t n, uint32_t op) {
     (void)ctx;
     return set_status(ops_unary((const float *)src, (float *)dst, n, op, ops::t_stream));

@@ -506,7 +506,13 @@ hipError_t hipLaunchKernel(const void *func, vkf_dim3 gridDim, vkf_dim3 blockDim
     // in the reference's order and argument positions.  Element counts that
     // come from the launch grid are clamped to the destination's allocation
     // when the allocation table knows it.
-    vkflame_set_stream(stream);
+    // These entry points take the calling thread's stream: set it to the
+    // launch's stream for this call and put the caller's back afterwards.
+    struct StreamScope {
+        void *prev;
+        explicit StreamScope(void *s) : prev(vkflame_get_stream()) { vkflame_set_stream(s); }
+        ~StreamScope() { vkflame_set_stream(prev); }
+    } stream_scope(stream);
     auto avail = [&](const void *p, uint64_t n, size_t es) {
         void *base = nullptr;
         size_t size = 0;

@@ -60,6 +60,7 @@ _SIGS = {
     "vkflame_chain_status": ([C.c_void_p, C.c_void_p], C.c_int),
     "vkflame_chain_destroy": ([C.c_void_p], C.c_int),
     "vkflame_set_stream": ([C.c_void_p], C.c_int),
+    "vkflame_get_stream": ([], C.c_void_p),
     "vkflame_dispatch_elementwise_f32": ([C.c_void_p] * 3 + [C.c_uint32] * 2, C.c_int),
     "vkflame_dispatch_scale_f32": ([C.c_void_p] * 3 + [C.c_uint32, C.c_float, C.c_float], C.c_int),
     "vkflame_dispatch_binop_f32": ([C.c_void_p] * 4 + [C.c_uint32] * 3, C.c_int),
