@@ -709,8 +709,11 @@ extern "C" int vkflame_chain_create(const vkf_chain_linear_t *lin, int n, int wo
             L[i].X = (const uint8_t *)src.y_rank[rank] - (int64_t)rank * (src.N / 2) * 8;
         }
     }
+    // Both run on the legacy default stream, which does not order itself
+    // before a non-blocking stream's chain launch: finish them here.
     if (cudaMemset(mem, 0, total) != cudaSuccess ||
-        cudaMemcpy(mem, L.data(), sizeof(Lin) * n, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaMemcpy(mem, L.data(), sizeof(Lin) * n, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess) {
         cudaFree(mem);
         return set_status(VKF_ERR_CUDA);
     }

@@ -66,12 +66,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: gives up after ~2^22 polls (each poll may suspend for a
-// hardware-defined time), ORs VKF_KERR_WAIT_TIMEOUT into *err and returns
-// false.  Callers then stop issuing work and exit.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wall-clock limit of every bounded wait in these kernels.  A count of polls
+// alone does not bound the time: each try_wait may suspend the thread for a
+// hardware-defined interval, so 2^22 of them can take minutes.
+constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;
+
+// Bounded wait: gives up once WAIT_LIMIT_NS of global-timer time has passed
+// (the timer is read only after the first 1024 polls, so waits that succeed
+// soon never read it), ORs VKF_KERR_WAIT_TIMEOUT into *err and returns false.
+// Callers then stop issuing work and exit.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned *err) {
-    for (uint32_t i = 0; i < (1u << 22); ++i)
+    for (int i = 0; i < 1024; ++i)
         if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    do {
+        for (int i = 0; i < 256; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+    } while (globaltimer_ns() - t0 < WAIT_LIMIT_NS);
     if (err) atomicOr(err, VKF_KERR_WAIT_TIMEOUT);
     return false;
 }

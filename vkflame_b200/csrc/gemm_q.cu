@@ -376,11 +376,18 @@ __device__ __forceinline__ int row_of_group(int g) {
     else return hi + 4 * lo;
 }
 
+// A later part's published flag; gives up after WAIT_LIMIT_NS like mbar_wait.
 __device__ __forceinline__ bool wait_flag(const int *f, unsigned *err) {
-    for (uint32_t i = 0; i < (1u << 24); ++i) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; ++i) {
         int v;
         asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
         if (v) return true;
+        if ((i & 255) == 0) {
+            const uint64_t t = globaltimer_ns();
+            if (i == 0) t0 = t;
+            else if (t - t0 >= WAIT_LIMIT_NS) break;
+        }
         __nanosleep(64);
     }
     if (err) atomicOr(err, VKF_KERR_WAIT_TIMEOUT);

@@ -86,7 +86,8 @@ DeviceState *device_state() {
     st->cc_minor = prop.minor;
     st->smem_optin = prop.sharedMemPerBlockOptin;
     if (cudaMalloc(&st->d_error, sizeof(unsigned)) != cudaSuccess ||
-        cudaMemset(st->d_error, 0, sizeof(unsigned)) != cudaSuccess) {
+        cudaMemset(st->d_error, 0, sizeof(unsigned)) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess) {  // zeroed before any kernel on any stream uses it
         delete st;
         return nullptr;
     }
@@ -126,7 +127,11 @@ static void *arena_get(std::map<std::pair<int, cudaStream_t>, Arena> &tab, cudaS
     }
     void *p = nullptr;
     if (cudaMalloc(&p, want) != cudaSuccess) return nullptr;
-    if (cudaMemset(p, 0, want) != cudaSuccess) {
+    // Zeroed on the stream that uses it: a plain cudaMemset runs on the
+    // legacy default stream, which does not order itself before work on a
+    // non-blocking stream, so a kernel could set a flag the late memset
+    // then clears.
+    if (cudaMemsetAsync(p, 0, want, stream) != cudaSuccess) {
         cudaFree(p);
         return nullptr;
     }
