@@ -331,7 +331,7 @@ class Stack:
         import torch
         from vkflame_b200 import shard
         if self.mode == "independent":
-            return None
+            return self._parity_independent()
         ep = self.runs()
         words = [lk[5].tensor[ep & 1] for lk in self.links]  # [1][N/2][2] int32
         sums = []
@@ -375,6 +375,36 @@ class Stack:
                                "reference": "vkflame_quant_linear_ex on the full weights (one GPU)",
                                "pass": bool(finite) and len(finite) == len(errs) and worst < tol}
         return out
+
+
+    def _parity_independent(self):
+        """Independent form (one rank): the first layer's five links, the
+        last layer's five and the head, each run again through the decode
+        GEMV (vkflame_quant_linear_ex) on the same weights and input row,
+        against the chain kernel's plain fp16 output; normwise
+        max |y - r| / max |r|.  The last layer's links read an input row
+        the kernel has kept resident across the whole stack."""
+        import torch
+        L = len(self.links)
+        sample = sorted(set(range(min(5, L))) | set(range(max(0, L - 6), L)))
+        errs = {}
+        for i in sample:
+            name, q, K, n, w, y, _ = self.links[i]
+            xin = self.x_h if K == HIDDEN else self.x_f
+            ref = torch.empty((1, n), device="cuda", dtype=torch.float16)
+            self.rt.quant_linear_ex(w.data_ptr(), q, xin.data_ptr(), self.rt.X_F16, ref.data_ptr(),
+                                    self.rt.Y_F16, 1, n, K, K, n, 0, self.stream)
+            torch.cuda.synchronize()
+            r, got = ref.double(), y.double()
+            errs[f"{name}#{i}"] = float((got - r).abs().max() / r.abs().max().clamp_min(1e-30))
+        tol = 1e-3
+        finite = {k: v for k, v in errs.items() if np.isfinite(v)}
+        worst = max(finite.values()) if finite else float("nan")
+        return {"runs": self.runs(), "vs_gemv": {
+            "links": errs, "max_normwise_err": worst, "tol": tol,
+            "nonfinite": sorted(k for k in errs if k not in finite),
+            "reference": "vkflame_quant_linear_ex on the same weights and input (one launch per link)",
+            "pass": bool(finite) and len(finite) == len(errs) and worst < tol}}
 
 
 def timed_graph(graph, stream, steps):
