@@ -200,3 +200,42 @@ def test_quant_linear_prefill_config4_size(rt):
     ref = xdq.astype(np.float64) @ wf.T
     assert G.normwise_err(y[rows], ref) < G.REL_TOL
     rt.check_kernel_errors()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("q,M,N,K", [(S.Q4_K, 512, 5120, 5120), (S.Q6_K, 256, 640, 13824)])
+def test_quant_linear_prefill_fresh_streams(rt, q, M, N, K):
+    """Stream-K tiles on streams the library has not seen: each call on a new
+    non-blocking stream makes the library create that stream's scratch and
+    flag arenas, whose zeroing must be ordered before the GEMM's first flag
+    store on that stream.  Every result equals, byte for byte, the same call
+    on a stream whose arenas already exist (the partial sums of a split tile
+    are added in a fixed order)."""
+    import torch
+    from cuda.bindings import runtime as cr
+    w = S.quant_matrix(q, N, K, seed=90 + q)
+    x = S.normal_f16((M, K), seed=91)
+    wd, xd = G.dev(w), G.dev(x)
+
+    def run(stream):
+        yd = torch.empty(M * N, dtype=torch.float16, device="cuda")
+        rt.quant_linear_ex(wd.data_ptr(), q, xd.data_ptr(), rt.X_F16, yd.data_ptr(), rt.Y_F16, M, N, K, K, N,
+                           rt.FLAG_STATIC_WEIGHTS, stream)
+        torch.cuda.synchronize()
+        return yd.cpu().numpy()
+
+    warm = torch.cuda.Stream()
+    run(warm.cuda_stream)
+    ref = run(warm.cuda_stream)
+    streams = []
+    try:
+        for _ in range(6):
+            err, s = cr.cudaStreamCreateWithFlags(cr.cudaStreamNonBlocking)
+            assert err == cr.cudaError_t.cudaSuccess
+            streams.append(s)
+            assert np.array_equal(run(int(s)).view(np.uint16), ref.view(np.uint16))
+        rt.check_kernel_errors()
+    finally:
+        torch.cuda.synchronize()
+        for s in streams:
+            cr.cudaStreamDestroy(s)
