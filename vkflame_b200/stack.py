@@ -17,6 +17,8 @@ Formats: Q4_K, Q5_K and Q6_K (the Q4_K_M family); another format raises.
 """
 from __future__ import annotations
 
+import warnings
+
 import numpy as np
 
 from . import gguf, rt, shard
@@ -93,7 +95,10 @@ class GGUFStack:
             rows = np.concatenate([self.file.weight(t)[3] for t in tensors]) if len(tensors) > 1 else \
                 self.file.weight(tensors[0])[3]
             r0, r1 = shard.row_range(N, world, rank)
-            w = torch.from_numpy(np.ascontiguousarray(rows[r0:r1]).reshape(-1)).cuda()
+            with warnings.catch_warnings():
+                # a read-only view of the mapped file, only read (copied to the device)
+                warnings.simplefilter("ignore", UserWarning)
+                w = torch.from_numpy(np.ascontiguousarray(rows[r0:r1]).reshape(-1)).cuda()
             self.weights.append(w)
             self.weight_bytes += w.numel()
             out = self.gg.buffer(N)
@@ -114,7 +119,12 @@ class GGUFStack:
         row (hidden values), copied in first when given."""
         import torch
         if x is not None:
-            self.x.copy_(torch.as_tensor(np.asarray(x, np.float16).reshape(1, -1)), non_blocking=True)
+            row = torch.as_tensor(np.asarray(x, np.float16).reshape(1, -1))
+            # the copy goes on the chain's own stream, so the kernel reads it
+            # after it lands whatever stream torch has current
+            s = torch.cuda.ExternalStream(self.stream) if self.stream else torch.cuda.default_stream()
+            with torch.cuda.stream(s):
+                self.x.copy_(row)
         self.chain.run(self.stream)
 
     def output(self, name: str = "head") -> np.ndarray:
